@@ -1,0 +1,479 @@
+// gemm_tc.cu -- K2: W8A8 GEMM on the 5th-generation tensor cores (sm_100a).
+//
+//   acc[m,n] = sum_k A[m,k] * B[n,k]                   int8 x int8 -> int32 (TMEM)
+//   out[m,n] = ((f32(acc) * sa[m|0]) * sb[n]) + bias[n]  fp32 epilogue -> out dtype
+//
+// Replaces quantization/w8a8_triton_kernels.py:174-318 (_w8a8_scaled_mm[_nomask]_kernel),
+// :67-171 (_int8_mm_no_scale[_nomask]_kernel) and kernels/quantization.py:38-105
+// (_w8a8_matmul_kernel).  The epilogue performs the reference's fp32 steps one
+// rounded op at a time, so int32 accumulators and the scaled outputs are
+// bit-identical to the reference's arithmetic.
+//
+// Design (one CTA per SM, persistent over 128x256 output tiles):
+//   warp 0      TMA producer: 128-byte-swizzled A[128x128B] and B[256x128B]
+//               tiles into a 4-stage shared-memory ring (48 KB per stage);
+//               A is streamed with an L2 evict-first policy, B (the 7.3 MB
+//               weight, reused by every tile) with evict-last.
+//   warp 1      MMA issuer: allocates 512 TMEM columns (two 128x256 int32
+//               accumulators), issues tcgen05.mma.cta_group::1.kind::i8
+//               (M=128, N=256, K=32) from one thread, frees ring slots with
+//               tcgen05.commit -> mbarrier.
+//   warps 2-5   epilogue: tcgen05.ld 32x32b of the finished accumulator,
+//               dequant + bias in fp32, vector stores; releases the TMEM
+//               buffer so the MMA warp overlaps the next tile's main loop.
+// No thread-block clusters and no multicast loads are used.  Every mbarrier
+// wait is bounded (common.cuh): on timeout the kernel records a watchdog code,
+// drains what it issued and returns instead of hanging.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace rb {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // K bytes per stage = one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int MMA_K = 32;  // int8 K per tcgen05.mma
+constexpr int A_BYTES = BM * BK;
+constexpr int B_BYTES = BN * BK;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 512;
+constexpr int NUM_THREADS = 192;
+constexpr int EPI_THREADS = 128;
+constexpr int BAR_BYTES = 256;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+
+// instruction descriptor: D=S32 (bits 4-5 = 2), A/B signed int8 (bits 7-9, 10-12 = 1),
+// both K-major, N>>3 at bit 17, M>>4 at bit 24
+constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                           ((uint32_t)(BM >> 4) << 24);
+
+struct EpiParams {
+  const void* sa;
+  const void* sb;
+  const void* bias;
+  void* out;
+  int64_t ldo;
+  int64_t M, N, K;
+  int sa_dtype, sa_per_row, sb_dtype, bias_dtype, out_dtype;
+};
+
+// K-major operand tile in shared memory with 128-byte swizzle: rows of 128 B,
+// 8-row groups 1024 B apart (SBO), LBO unused (1), version 1, layout 2.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int c0, int c1, uint32_t bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Epilogue for 32 consecutive columns of one row.
+__device__ __forceinline__ void epilogue_32(const uint32_t* r, int64_t row, int64_t col0, float sa_v,
+                                            const EpiParams& ep) {
+  const int64_t N = ep.N;
+  const int ncol = (N - col0 < 32) ? (int)(N - col0) : 32;
+  if (ep.out_dtype == RB_I32) {
+    int32_t* dst = reinterpret_cast<int32_t*>(ep.out) + row * ep.ldo + col0;
+    if (ncol == 32 && aligned(dst, 16)) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+    } else {
+      for (int j = 0; j < ncol; ++j) dst[j] = (int32_t)r[j];
+    }
+    return;
+  }
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float x = __int2float_rn((int)r[j]);
+    x = __fmul_rn(x, sa_v);
+    v[j] = x;
+  }
+  if (ncol == 32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(v[j], load_as_f32(ep.sb, ep.sb_dtype, col0 + j));
+    if (ep.bias != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], load_as_f32(ep.bias, ep.bias_dtype, col0 + j));
+    }
+  } else {
+    for (int j = 0; j < ncol; ++j) {
+      v[j] = __fmul_rn(v[j], load_as_f32(ep.sb, ep.sb_dtype, col0 + j));
+      if (ep.bias != nullptr) v[j] = __fadd_rn(v[j], load_as_f32(ep.bias, ep.bias_dtype, col0 + j));
+    }
+  }
+  if (ep.out_dtype == RB_F32) {
+    float* dst = reinterpret_cast<float*>(ep.out) + row * ep.ldo + col0;
+    if (ncol == 32 && aligned(dst, 16)) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+      for (int j = 0; j < ncol; ++j) dst[j] = v[j];
+    }
+  } else {
+    uint16_t* dst = reinterpret_cast<uint16_t*>(ep.out) + row * ep.ldo + col0;
+    const bool bf = ep.out_dtype == RB_BF16;
+    if (ncol == 32 && aligned(dst, 16)) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 w;
+        w.x = bf ? pack_bf16x2(v[j], v[j + 1]) : pack_f16x2(v[j], v[j + 1]);
+        w.y = bf ? pack_bf16x2(v[j + 2], v[j + 3]) : pack_f16x2(v[j + 2], v[j + 3]);
+        w.z = bf ? pack_bf16x2(v[j + 4], v[j + 5]) : pack_f16x2(v[j + 4], v[j + 5]);
+        w.w = bf ? pack_bf16x2(v[j + 6], v[j + 7]) : pack_f16x2(v[j + 6], v[j + 7]);
+        *reinterpret_cast<uint4*>(dst + j) = w;
+      }
+    } else {
+      for (int j = 0; j < ncol; ++j) {
+        if (bf) {
+          __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
+          dst[j] = *reinterpret_cast<uint16_t*>(&h);
+        } else {
+          __half h = __float2half_rn(v[j]);
+          dst[j] = *reinterpret_cast<uint16_t*>(&h);
+        }
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    w8a8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ EpiParams ep) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;                // [STAGES]  TMA -> MMA
+  uint64_t* empty = bars + STAGES;      // [STAGES]  MMA -> TMA
+  uint64_t* tfull = bars + 2 * STAGES;  // [2]       MMA -> epilogue
+  uint64_t* tempty = tfull + 2;         // [2]       epilogue -> MMA
+  uint64_t* done = tempty + 2;          // [1]       MMA drain at exit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&tfull[b]), 1);
+      mbar_init(smem_u32(&tempty[b]), EPI_THREADS);
+    }
+    mbar_init(smem_u32(done), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int64_t m_tiles = (ep.M + BM - 1) / BM;
+  const int64_t n_tiles = (ep.N + BN - 1) / BN;
+  const int64_t num_tiles = m_tiles * n_tiles;
+  const int kblocks = (int)((ep.K + BK - 1) / BK);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      const uint64_t pol_a = policy_evict_first(), pol_b = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, issued_phase = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (int)((tile / n_tiles) * BM);
+        const int n0 = (int)((tile % n_tiles) * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, kWaitTimeoutProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmA, kb * BK, m0, fb, pol_a);
+          tma_load_2d(smem_u32(sB + stage * B_BYTES), &tmB, kb * BK, n0, fb, pol_b);
+          issued |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // never leave a bulk copy in flight behind an exiting CTA
+      for (int s = 0; s < STAGES; ++s)
+        if (issued & (1u << s))
+          mbar_wait_bounded(smem_u32(&full[s]), (issued_phase >> s) & 1u, kWaitTimeoutProducer, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // --------------------------------------------------------------- MMA
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1, kWaitTimeoutMma, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&full[stage]), phase, kWaitTimeoutMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = sw128_desc(smem_u32(sA + stage * A_BYTES));
+          const uint64_t bdesc = sw128_desc(smem_u32(sB + stage * B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / MMA_K; ++k)
+            umma_i8(d_tmem, adesc + (uint64_t)(k * MMA_K / 16), bdesc + (uint64_t)(k * MMA_K / 16),
+                    (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(smem_u32(&empty[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&tfull[acc]));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // all MMAs issued by this thread are complete once `done` flips
+      umma_commit(smem_u32(done));
+      mbar_wait_bounded(smem_u32(done), 0, kWaitTimeoutMma, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 are reachable from this warp
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int64_t m0 = (tile / n_tiles) * BM;
+      const int64_t n0 = (tile % n_tiles) * BN;
+      if (!mbar_wait_bounded(smem_u32(&tfull[acc]), acc_phase, kWaitTimeoutEpilogue, abort_flag)) break;
+      tc_fence_after();
+      const int64_t row = m0 + quarter * 32 + lane;
+      float sa_v = 0.0f;
+      if (row < ep.M && ep.out_dtype != RB_I32)
+        sa_v = load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? row : 0);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int64_t col0 = n0 + c * 32;
+        if (col0 >= ep.N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+        if (row < ep.M) epilogue_32(r, row, col0, sa_v, ep);
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&tempty[acc]));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// CUDA-core GEMM for shapes the tensor-map path cannot take (K % 16 != 0,
+// unaligned operands, K == 0).  One thread per output element.
+__global__ void w8a8_gemm_simple_kernel(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
+                                        const __grid_constant__ EpiParams ep) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= ep.M * ep.N) return;
+  const int64_t m = idx / ep.N, n = idx % ep.N;
+  int32_t acc = 0;
+  const int8_t* a = A + m * lda;
+  const int8_t* b = B + n * ldb;
+  for (int64_t k = 0; k < ep.K; ++k) acc += (int32_t)a[k] * (int32_t)b[k];
+  if (ep.out_dtype == RB_I32) {
+    reinterpret_cast<int32_t*>(ep.out)[m * ep.ldo + n] = acc;
+    return;
+  }
+  float v = __int2float_rn(acc);
+  v = __fmul_rn(v, load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? m : 0));
+  v = __fmul_rn(v, load_as_f32(ep.sb, ep.sb_dtype, n));
+  if (ep.bias != nullptr) v = __fadd_rn(v, load_as_f32(ep.bias, ep.bias_dtype, n));
+  if (ep.out_dtype == RB_F32) {
+    reinterpret_cast<float*>(ep.out)[m * ep.ldo + n] = v;
+  } else if (ep.out_dtype == RB_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(ep.out)[m * ep.ldo + n] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<__half*>(ep.out)[m * ep.ldo + n] = __float2half_rn(v);
+  }
+}
+
+// --------------------------------------------------------------------- host
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode;
+}
+
+static int make_tmap(CUtensorMap* tm, const int8_t* base, int64_t inner, int64_t outer, int64_t ld_bytes,
+                     uint32_t box_inner, uint32_t box_outer) {
+  auto enc = encode_fn();
+  if (enc == nullptr) return fail(RB_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)ld_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(RB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return RB_OK;
+}
+
+static std::once_flag g_attr_once[64];
+
+}  // namespace tc
+}  // namespace rb
+
+using namespace rb;
+
+extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M, int64_t N,
+                            int64_t K, const void* sa, int sa_dtype, int sa_per_row, const void* sb, int sb_dtype,
+                            const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
+                            void* stream) {
+  using namespace rb::tc;
+  if (M < 0 || N < 0 || K < 0) return fail(RB_ERR_VALUE, "negative GEMM shape");
+  if (M == 0 || N == 0) return RB_OK;
+  if (A == nullptr || B == nullptr || out == nullptr) return fail(RB_ERR_VALUE, "null operand");
+  if (lda < K || ldb < K || ldo < N) return fail(RB_ERR_VALUE, "leading dimension smaller than the row");
+  if (out_dtype != RB_BF16 && out_dtype != RB_F16 && out_dtype != RB_F32 && out_dtype != RB_I32)
+    return fail(RB_ERR_VALUE, "out dtype must be bf16/f16/f32/i32");
+  if (out_dtype != RB_I32) {
+    if (sa == nullptr || sb == nullptr) return fail(RB_ERR_VALUE, "scales must be given");
+    auto fdt = [](int d) { return d == RB_F32 || d == RB_BF16 || d == RB_F16; };
+    if (!fdt(sa_dtype) || !fdt(sb_dtype) || (bias != nullptr && !fdt(bias_dtype)))
+      return fail(RB_ERR_VALUE, "scale/bias dtypes must be f32/bf16/f16");
+  }
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL) return fail(RB_ERR_UNSUPPORTED, "dimension above 2^31-1");
+  EpiParams ep;
+  ep.sa = sa;
+  ep.sb = sb;
+  ep.bias = bias;
+  ep.out = out;
+  ep.ldo = ldo;
+  ep.M = M;
+  ep.N = N;
+  ep.K = K;
+  ep.sa_dtype = sa_dtype;
+  ep.sa_per_row = sa_per_row;
+  ep.sb_dtype = sb_dtype;
+  ep.bias_dtype = bias_dtype;
+  ep.out_dtype = out_dtype;
+  cudaStream_t st = (cudaStream_t)stream;
+
+  const bool tma_ok = K > 0 && K % 16 == 0 && lda % 16 == 0 && ldb % 16 == 0 && aligned(A, 16) &&
+                      aligned(B, 16) && device_is_sm100();
+  if (!tma_ok) {
+    if (!device_is_sm100()) return fail(RB_ERR_DEVICE, "rb_w8a8_gemm needs an sm_100 (B200) device");
+    const int64_t total = M * N;
+    const int threads = 256;
+    w8a8_gemm_simple_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(A, lda, B, ldb, ep);
+    return check_cuda(cudaGetLastError(), "w8a8_gemm_simple_kernel launch");
+  }
+  CUtensorMap tmA, tmB;
+  int rc = make_tmap(&tmA, A, K, M, lda, BK, BM);
+  if (rc) return rc;
+  rc = make_tmap(&tmB, B, K, N, ldb, BK, BN);
+  if (rc) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(g_attr_once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(w8a8_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return check_cuda(attr_err, "cudaFuncSetAttribute(w8a8_gemm_tc_kernel)");
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = (int)std::min<int64_t>(tiles, sm_count());
+  w8a8_gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tmA, tmB, ep);
+  return check_cuda(cudaGetLastError(), "w8a8_gemm_tc_kernel launch");
+}

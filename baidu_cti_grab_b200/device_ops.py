@@ -1,0 +1,256 @@
+"""torch-facing wrappers of the C ABI: validate tensors, pass device pointers
+and the current stream, allocate outputs with torch's caching allocator.
+
+These are the only functions in the package that call into librep_b200.so;
+the reference-shaped modules (w8a8_triton_kernels, quantization,
+rep_encoder_fusion, rep_encoder) are built on them.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib as L
+
+_DT = {
+    torch.float32: L.RB_F32,
+    torch.bfloat16: L.RB_BF16,
+    torch.float16: L.RB_F16,
+    torch.int32: L.RB_I32,
+    torch.int8: L.RB_I8,
+}
+
+
+def rb_dtype(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}") from None
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def require_cuda(name: str, *tensors: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} expects CUDA tensors")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"{name}: tensors on different devices ({dev} vs {t.device})")
+    if dev is None:
+        raise RuntimeError(f"{name} expects CUDA tensors")
+    return dev
+
+
+# --------------------------------------------------------------- RepEncoder
+def rep_gather_ln_quant(table: torch.Tensor, slot_values: Sequence[torch.Tensor],
+                        slot_offsets: Sequence[torch.Tensor], gamma: torch.Tensor, beta: torch.Tensor,
+                        eps: float, act_mode: str = "dynamic", static_scale: Optional[torch.Tensor] = None,
+                        q_out: Optional[torch.Tensor] = None, scale_out: Optional[torch.Tensor] = None,
+                        want_pooled: bool = False, want_ln: bool = False):
+    """Fused gather -> pool -> concat -> LayerNorm -> int8 (rb_rep_gather_ln_quant).
+
+    Returns (q int8[N, S*512] or None, scale fp32[N] or None, pooled or None, ln or None)."""
+    S = len(slot_values)
+    dev = require_cuda("rep_gather_ln_quant", table, gamma, beta, *slot_values, *slot_offsets)
+    if len(slot_offsets) != S:
+        raise ValueError("slot_values and slot_offsets differ in length")
+    if table.dim() != 2 or not table.is_contiguous():
+        raise ValueError("table must be a contiguous [V, 512] tensor")
+    n_items = int(slot_offsets[0].numel()) - 1 if S else 0
+    for s in range(S):
+        if slot_values[s].dtype != torch.int64 or slot_offsets[s].dtype != torch.int64:
+            raise ValueError("slot values and offsets must be int64")
+        if not slot_values[s].is_contiguous() or not slot_offsets[s].is_contiguous():
+            raise ValueError("slot values and offsets must be contiguous")
+        if slot_offsets[s].numel() - 1 != n_items:
+            raise ValueError("every slot needs offsets of length N+1")
+    H = S * table.shape[1]
+    mode = {"dynamic": L.RB_ACT_DYNAMIC, "static": L.RB_ACT_STATIC, "none": L.RB_ACT_NONE}[act_mode]
+    q = scale = None
+    if mode != L.RB_ACT_NONE:
+        q = torch.empty((n_items, H), dtype=torch.int8, device=dev) if q_out is None else q_out
+        if mode == L.RB_ACT_DYNAMIC:
+            scale = torch.empty((n_items,), dtype=torch.float32, device=dev) if scale_out is None else scale_out
+    pooled = torch.empty((n_items, H), dtype=table.dtype, device=dev) if want_pooled else None
+    ln = torch.empty((n_items, H), dtype=table.dtype, device=dev) if (want_ln or mode == L.RB_ACT_NONE) else None
+    gamma = gamma.contiguous()
+    beta = beta.contiguous()
+    if static_scale is not None:
+        static_scale = static_scale.contiguous()
+    with torch.cuda.device(dev):
+        L.call("rb_rep_gather_ln_quant", table.data_ptr(), rb_dtype(table), table.shape[0], table.shape[1],
+               L.ptr_array([v.data_ptr() for v in slot_values]),
+               L.ptr_array([o.data_ptr() for o in slot_offsets]),
+               L.i64_array([v.numel() for v in slot_values]), S, n_items,
+               gamma.data_ptr(), beta.data_ptr(), rb_dtype(gamma), float(eps), mode,
+               _ptr(static_scale), rb_dtype(static_scale) if static_scale is not None else 0,
+               _ptr(q), H if q is None else q.stride(0), _ptr(scale), _ptr(pooled), _ptr(ln), _stream(dev))
+    return q, scale, pooled, ln
+
+
+def rep_gather_pool(table: torch.Tensor, slot_values: Sequence[torch.Tensor],
+                    slot_offsets: Sequence[torch.Tensor], col_slot: Sequence[int], width_slots: int,
+                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Gather + sum-pool of a subset of slots into columns col_slot[j]*512 of [N, width_slots*512]."""
+    S = len(slot_values)
+    dev = require_cuda("rep_gather_pool", table, *slot_values, *slot_offsets)
+    n_items = int(slot_offsets[0].numel()) - 1
+    D = table.shape[1]
+    if out is None:
+        out = torch.empty((n_items, width_slots * D), dtype=table.dtype, device=dev)
+    with torch.cuda.device(dev):
+        L.call("rb_rep_gather_pool", table.data_ptr(), rb_dtype(table), table.shape[0], D,
+               L.ptr_array([v.data_ptr() for v in slot_values]),
+               L.ptr_array([o.data_ptr() for o in slot_offsets]),
+               L.i64_array([v.numel() for v in slot_values]), L.i32_array(col_slot), S, n_items,
+               out.data_ptr(), out.stride(0), _stream(dev))
+    return out
+
+
+def layernorm_quant(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float,
+                    act_mode: str = "dynamic", static_scale: Optional[torch.Tensor] = None,
+                    want_ln: bool = False):
+    """LayerNorm (+ int8 quantisation) of dense rows x[N, S*512] (rb_layernorm_quant)."""
+    dev = require_cuda("layernorm_quant", x, gamma, beta)
+    if x.dim() != 2 or x.shape[1] % 512 != 0:
+        raise ValueError("layernorm_quant expects x as [N, S*512]")
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    n, H = x.shape
+    S = H // 512
+    mode = {"dynamic": L.RB_ACT_DYNAMIC, "static": L.RB_ACT_STATIC, "none": L.RB_ACT_NONE}[act_mode]
+    q = torch.empty((n, H), dtype=torch.int8, device=dev) if mode != L.RB_ACT_NONE else None
+    scale = torch.empty((n,), dtype=torch.float32, device=dev) if mode == L.RB_ACT_DYNAMIC else None
+    ln = torch.empty((n, H), dtype=x.dtype, device=dev) if (want_ln or mode == L.RB_ACT_NONE) else None
+    gamma = gamma.contiguous()
+    beta = beta.contiguous()
+    if static_scale is not None:
+        static_scale = static_scale.contiguous()
+    with torch.cuda.device(dev):
+        L.call("rb_layernorm_quant", x.data_ptr(), rb_dtype(x), n, S, x.stride(0), gamma.data_ptr(),
+               beta.data_ptr(), rb_dtype(gamma), float(eps), mode, _ptr(static_scale),
+               rb_dtype(static_scale) if static_scale is not None else 0, _ptr(q), H, _ptr(scale), _ptr(ln),
+               _stream(dev))
+    return q, scale, ln
+
+
+# ------------------------------------------------------------- quantisers
+def quant_dynamic_per_token_out(x2d: torch.Tensor, xq: torch.Tensor, scale: torch.Tensor):
+    dev = require_cuda("dynamic_per_token_quantize_activation", x2d, xq, scale)
+    if x2d.dim() != 2 or x2d.stride(1) != 1 or xq.stride(1) != 1:
+        raise ValueError("expected 2-D row-major x and xq")
+    M, K = x2d.shape
+    with torch.cuda.device(dev):
+        L.call("rb_quant_dynamic_per_token", x2d.data_ptr(), rb_dtype(x2d), M, K, x2d.stride(0), xq.data_ptr(),
+               xq.stride(0), scale.data_ptr(), _stream(dev))
+    return xq, scale
+
+
+def quant_static_out(x: torch.Tensor, scale: torch.Tensor, xq: torch.Tensor) -> torch.Tensor:
+    dev = require_cuda("static_quantize_activation", x, scale, xq)
+    if not x.is_contiguous() or not xq.is_contiguous():
+        raise ValueError("static quantisation expects contiguous tensors")
+    with torch.cuda.device(dev):
+        L.call("rb_quant_static", x.data_ptr(), rb_dtype(x), x.numel(), scale.data_ptr(), rb_dtype(scale),
+               xq.data_ptr(), _stream(dev))
+    return xq
+
+
+def quant_rows_v1(x2d: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    dev = require_cuda("quantize_rows_int8", x2d)
+    M, K = x2d.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=dev)
+    s = torch.empty((M,), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        L.call("rb_quant_rows_v1", x2d.data_ptr(), rb_dtype(x2d), M, K, x2d.stride(0), q.data_ptr(), K,
+               s.data_ptr(), _stream(dev))
+    return q, s
+
+
+def quantize_weight_per_channel(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """W[N,K] -> (q int8 [N,K] K-contiguous, scale fp32 [N])."""
+    dev = require_cuda("quantize_weight_per_channel", w)
+    if w.dim() != 2:
+        raise ValueError("expected W as [N, K]")
+    if w.stride(1) != 1:
+        w = w.contiguous()
+    N, K = w.shape
+    q = torch.empty((N, K), dtype=torch.int8, device=dev)
+    s = torch.empty((N,), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        L.call("rb_quantize_weight_per_channel", w.data_ptr(), rb_dtype(w), N, K, w.stride(0), q.data_ptr(),
+               s.data_ptr(), _stream(dev))
+    return q, s
+
+
+def pack_weight_nk(qweight_t: torch.Tensor) -> torch.Tensor:
+    """[K,N] int8 view (any strides) -> [N,K] K-contiguous int8 copy."""
+    dev = require_cuda("pack_weight_nk", qweight_t)
+    K, N = qweight_t.shape
+    dst = torch.empty((N, K), dtype=torch.int8, device=dev)
+    with torch.cuda.device(dev):
+        L.call("rb_pack_weight_nk", qweight_t.data_ptr(), K, N, qweight_t.stride(0), qweight_t.stride(1),
+               dst.data_ptr(), _stream(dev))
+    return dst
+
+
+def as_nk(qweight_t: torch.Tensor) -> torch.Tensor:
+    """The K-contiguous [N,K] view of a [K,N] weight, repacking only when needed."""
+    K, N = qweight_t.shape
+    if qweight_t.stride(0) == 1 and qweight_t.stride(1) >= K and qweight_t.stride(1) % 16 == 0 \
+            and qweight_t.data_ptr() % 16 == 0:
+        return qweight_t.t()
+    return pack_weight_nk(qweight_t)
+
+
+# ------------------------------------------------------------------- GEMM
+def w8a8_gemm(a: torch.Tensor, b_nk: torch.Tensor, scale_a: Optional[torch.Tensor],
+              scale_b: Optional[torch.Tensor], out: torch.Tensor, *, bias: Optional[torch.Tensor] = None,
+              sa_per_row: bool = True) -> torch.Tensor:
+    """out = ((f32(A @ B^T) * sa) * sb) + bias, or raw int32 when out is int32."""
+    dev = require_cuda("w8a8_gemm", a, b_nk, out, scale_a, scale_b, bias)
+    if a.dim() != 2 or b_nk.dim() != 2 or a.stride(1) != 1 or b_nk.stride(1) != 1 or out.stride(1) != 1:
+        raise ValueError("w8a8_gemm expects row-major 2-D operands")
+    M, K = a.shape
+    N = b_nk.shape[0]
+    if b_nk.shape[1] != K:
+        raise ValueError(f"shape mismatch: A K={K}, B K={b_nk.shape[1]}")
+    if tuple(out.shape) != (M, N):
+        raise ValueError(f"out must be [{M}, {N}]")
+    raw = out.dtype == torch.int32
+    if not raw:
+        scale_a = scale_a.contiguous()
+        scale_b = scale_b.contiguous()
+    if bias is not None:
+        bias = bias.contiguous()
+    with torch.cuda.device(dev):
+        L.call("rb_w8a8_gemm", a.data_ptr(), a.stride(0), b_nk.data_ptr(), b_nk.stride(0), M, N, K,
+               _ptr(scale_a), rb_dtype(scale_a) if scale_a is not None else 0, 1 if sa_per_row else 0,
+               _ptr(scale_b), rb_dtype(scale_b) if scale_b is not None else 0, _ptr(bias),
+               rb_dtype(bias) if bias is not None else 0, out.data_ptr(), out.stride(0), rb_dtype(out),
+               _stream(dev))
+    return out
+
+
+def device_error(reset: bool = False) -> int:
+    return L.device_error(reset)
+
+
+def selftest_wait_timeout(budget_ns: int, device=None) -> None:
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        L.call("rb_selftest_wait_timeout", int(budget_ns), _stream(dev))

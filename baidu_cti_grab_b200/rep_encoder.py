@@ -1,0 +1,163 @@
+"""RepEncoder on B200: the reference's models.RepEncoder (models.py:14-48) with
+the forward pass replaced by two sm_100a kernels.
+
+    K1  rb_rep_gather_ln_quant   28-slot embedding-bag gather + fp32 sum-pool +
+                                 concat + LayerNorm + int8 quantisation; the
+                                 [N, 14336] row never reaches HBM
+    K2  rb_w8a8_gemm             tcgen05 int8 GEMM [N,14336] x [14336,512] with
+                                 the dequant / bias epilogue fused
+
+``rep_encoder_forward(rep, batch)`` works on any module with the reference's
+attribute layout -- ``emb`` (nn.EmbeddingBag, mode='sum', padding_idx=0),
+``input_norm`` (nn.LayerNorm), ``linear`` (nn.Linear, or the reference's
+quantised ``StaticQuantizedLinear`` with ``qweight_t``/``weight_scale``/
+``static_act_scale``/``bias`` buffers) and ``slot_num`` -- so it serves the
+reference's own module instances unchanged.  ``install(models)`` adds the
+``fuse_mode == "b200"`` branch to the reference's RepEncoder.forward.
+
+Activation quantisation: with an fp ``nn.Linear`` the weight is quantised per
+output channel once (cached until the weight changes) and activations are
+quantised per token (dynamic, the default).  With the quantised checkpoint
+layer (``use_quant``) the stored static per-tensor scale is used, as the
+reference's StaticQuantizedLinear does.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, Optional, Sequence
+
+import torch
+import torch.nn as nn
+
+from . import device_ops
+
+FUSE_MODE = "b200"
+
+
+def _slot_tensors(batch, slot_num: int, device: torch.device):
+    values, offsets = [], []
+    for i in range(slot_num):
+        v, o = batch[i + 1]
+        if not torch.is_tensor(v):
+            v = torch.as_tensor(v)
+        if not torch.is_tensor(o):
+            o = torch.as_tensor(o)
+        if v.device != device:
+            v = v.to(device, non_blocking=True)
+        o = o.to(v.device)  # models.py:31
+        if v.dtype != torch.int64:
+            v = v.long()
+        if o.dtype != torch.int64:
+            o = o.long()
+        values.append(v.contiguous())
+        offsets.append(o.contiguous())
+    return values, offsets
+
+
+def _quantized_weight(rep: nn.Module):
+    """(w_nk int8 [N,K], w_scale [N], bias, static_scale or None) for rep.linear."""
+    lin = rep.linear
+    if getattr(lin, "use_quant", False):
+        from .w8a8_triton_kernels import _packed_nk
+        return _packed_nk(lin.qweight_t), lin.weight_scale, lin.bias, lin.static_act_scale
+    w = lin.weight
+    key = (w.data_ptr(), w._version, w.dtype, w.device)
+    cache = getattr(rep, "_b200_wcache", None)
+    if cache is None or cache[0] != key:
+        q_nk, w_scale = device_ops.quantize_weight_per_channel(w.detach())
+        cache = (key, q_nk, w_scale)
+        rep._b200_wcache = cache
+    return cache[1], cache[2], lin.bias, None
+
+
+def rep_encoder_forward(rep: nn.Module, batch, act_mode: Optional[str] = None,
+                        return_intermediates: bool = False):
+    """Fused B200 forward of a RepEncoder-shaped module on a reference batch dict.
+
+    Returns rep_emb [N, d_model] in the table dtype (and, with
+    return_intermediates, a dict with q, scale, pooled and ln)."""
+    table = rep.emb.weight
+    device = table.device
+    if device.type != "cuda":
+        raise RuntimeError("RepEncoder fuse_mode 'b200' expects the module on a CUDA device")
+    if rep.emb.mode != "sum" or rep.emb.padding_idx not in (0, None):
+        raise ValueError("fuse_mode 'b200' implements EmbeddingBag(mode='sum', padding_idx=0)")
+    values, offsets = _slot_tensors(batch, rep.slot_num, device)
+    w_nk, w_scale, bias, static_scale = _quantized_weight(rep)
+    if act_mode is None:
+        act_mode = "static" if static_scale is not None else "dynamic"
+    if act_mode == "static" and static_scale is None:
+        raise ValueError("act_mode 'static' needs a quantised linear with static_act_scale")
+    ln = rep.input_norm
+    if ln.weight is None or ln.bias is None:
+        raise ValueError("fuse_mode 'b200' needs an affine LayerNorm")
+    q, scale, pooled, ln_out = device_ops.rep_gather_ln_quant(
+        table.detach(), values, offsets, ln.weight.detach(), ln.bias.detach(), ln.eps, act_mode=act_mode,
+        static_scale=static_scale, want_pooled=return_intermediates, want_ln=return_intermediates)
+    n = q.shape[0]
+    out = torch.empty((n, w_nk.shape[0]), dtype=table.dtype, device=device)
+    sa = scale if act_mode == "dynamic" else static_scale
+    device_ops.w8a8_gemm(q, w_nk, sa, w_scale, out, bias=None if bias is None else bias.detach(),
+                         sa_per_row=(act_mode == "dynamic"))
+    if return_intermediates:
+        return out, {"q": q, "scale": scale, "pooled": pooled, "ln": ln_out}
+    return out
+
+
+class RepEncoder(nn.Module):
+    """Drop-in for models.RepEncoder whose forward runs the B200 kernels.
+
+    Constructor arguments and parameter names match the reference
+    (models.py:14-22), so its state dicts load unchanged."""
+
+    def __init__(self, vocab_size, emb_dim, padding_idx=0, slot_num=0, d_model=0, fuse_mode=FUSE_MODE,
+                 act_mode: Optional[str] = None):
+        super().__init__()
+        self.emb = nn.EmbeddingBag(num_embeddings=vocab_size, embedding_dim=emb_dim, padding_idx=padding_idx,
+                                   mode="sum")
+        self.emb_dim = emb_dim
+        self.slot_num = slot_num
+        self.fuse_mode = fuse_mode
+        self.act_mode = act_mode
+        self.input_norm = nn.LayerNorm(slot_num * emb_dim)
+        self.linear = nn.Linear(in_features=slot_num * emb_dim, out_features=d_model)
+
+    def forward(self, batch):
+        return rep_encoder_forward(self, batch, act_mode=self.act_mode)
+
+    @classmethod
+    def from_parts(cls, table: torch.Tensor, ln_weight: torch.Tensor, ln_bias: torch.Tensor,
+                   linear_weight: torch.Tensor, linear_bias: Optional[torch.Tensor], eps: float = 1e-5,
+                   act_mode: Optional[str] = None) -> "RepEncoder":
+        """Wrap existing device tensors (no copy): table [V, D], LayerNorm affine
+        [S*D], Linear weight [d_model, S*D] and bias [d_model]."""
+        V, D = table.shape
+        with torch.device("meta"):
+            m = cls(V, D, 0, ln_weight.numel() // D, linear_weight.shape[0], act_mode=act_mode)
+        m.emb.weight = nn.Parameter(table, requires_grad=False)
+        m.input_norm.weight = nn.Parameter(ln_weight, requires_grad=False)
+        m.input_norm.bias = nn.Parameter(ln_bias, requires_grad=False)
+        m.input_norm.eps = eps
+        m.linear.weight = nn.Parameter(linear_weight, requires_grad=False)
+        m.linear.bias = None if linear_bias is None else nn.Parameter(linear_bias, requires_grad=False)
+        return m
+
+
+def install(models_module) -> None:
+    """Add fuse_mode "b200" to a reference ``models`` module's RepEncoder.forward.
+
+    After ``install(models)``, ``models.load_model(..., rep_fuse_mode="b200")``
+    and ``infer.py --rep-fuse-mode b200`` run this package's kernels; every
+    other fuse mode keeps the reference's own code path."""
+    cls = models_module.RepEncoder
+    if getattr(cls, "_b200_installed", False):
+        return
+    original = cls.forward
+
+    def forward(self, batch):
+        if getattr(self, "fuse_mode", None) == FUSE_MODE:
+            return rep_encoder_forward(self, batch)
+        return original(self, batch)
+
+    cls.forward = forward
+    cls._b200_installed = True

@@ -1,0 +1,159 @@
+/*
+ * rep_b200.h -- C ABI of the B200 (sm_100a) RepEncoder W8A8 hot path.
+ *
+ * Plain pointers and sizes only; every device pointer refers to memory of the
+ * current CUDA device, and every call is asynchronous on `stream` (a
+ * cudaStream_t passed as void*; NULL = legacy default stream).  Calls return
+ * an rb_status; rb_last_error() gives the message of the last failure on the
+ * calling thread.  The library never allocates device memory.
+ *
+ * Each entry point names the reference interface it replaces (paths inside
+ * YuDeng0102/baidu_cti_grab).
+ */
+#ifndef REP_B200_H
+#define REP_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+enum rb_dtype { RB_F32 = 0, RB_BF16 = 1, RB_F16 = 2, RB_I32 = 3, RB_I8 = 4 };
+
+/* activation quantisation: dynamic per-token, static per-tensor, or none (LayerNorm output only) */
+enum rb_act_mode { RB_ACT_DYNAMIC = 0, RB_ACT_STATIC = 1, RB_ACT_NONE = 2 };
+
+/* return codes; the Python layer maps them to the reference's exception types */
+enum rb_status {
+  RB_OK = 0,
+  RB_ERR_VALUE = 1,       /* bad shape / argument  -> ValueError */
+  RB_ERR_UNSUPPORTED = 2, /* valid but not supported by this build -> ValueError */
+  RB_ERR_CUDA = 3,        /* CUDA runtime/driver error -> RuntimeError */
+  RB_ERR_DEVICE = 4       /* not an sm_100 device, or a device-side timeout -> RuntimeError */
+};
+
+/* maximum number of slots one call of the gather kernel takes */
+#define RB_MAX_SLOTS 32
+
+const char* rb_last_error(void);
+int rb_version(void);
+
+/* 1 when the current device is sm_100 and the library's kernels can launch on it. */
+int rb_device_supported(void);
+
+/*
+ * Device-side watchdog status: 0, or the code of the first bounded wait that
+ * ran out of time in one of this library's kernels since the last reset
+ * (kernels return instead of hanging).  Synchronous; reset=1 clears it.
+ */
+int rb_device_error(int reset);
+
+/* Test hook: run the GEMM pipeline's bounded mbarrier wait on a barrier that
+ * nothing arrives on, with a budget of `budget_ns`; sets the watchdog status. */
+int rb_selftest_wait_timeout(uint64_t budget_ns, void* stream);
+
+/*
+ * Fused gather -> sum-pool -> concat -> LayerNorm -> int8 quantisation.
+ * Replaces models.py:24-48 (RepEncoder.forward: 28x clamp + nn.EmbeddingBag
+ * (mode='sum', padding_idx=0) + torch.cat + nn.LayerNorm) followed by
+ * quantization/w8a8_triton_kernels.py:392-460 (quantize_activation, dynamic
+ * per-token or static per-tensor), without writing the concatenated row.
+ *
+ *   table            [num_rows, emb_dim] row-major, table_dtype RB_BF16 or RB_F32;
+ *                    emb_dim must be 512.  Ids are clamped to [0, num_rows-1]
+ *                    and id 0 is the padding row (excluded from the sum).
+ *   slot_values[s]   device int64 ids of slot s (nnz[s] of them)
+ *   slot_offsets[s]  device int64 [num_items+1]; bag i = [off[i], off[i+1]) for
+ *                    i < num_items-1 and [off[num_items-1], nnz[s]) for the last
+ *                    (the reference passes offsets[:-1]); ends clamp to nnz[s].
+ *   slot_nnz         host array [num_slots]
+ *   ln_gamma/ln_beta [num_slots*512] in ln_dtype (RB_BF16/RB_F32/RB_F16), eps
+ *   act_mode         RB_ACT_DYNAMIC: q_out + scale_out[num_items] (fp32)
+ *                    RB_ACT_STATIC:  q_out with 1/static_scale[0]
+ *                    RB_ACT_NONE:    no quantisation (ln_out required)
+ *   q_out            int8 [num_items, ldq] (ldq >= num_slots*512, multiple of 16)
+ *   pooled_out, ln_out  optional [num_items, num_slots*512] in table_dtype.
+ * The LayerNorm and the int8 values are computed in the row dtype (= table dtype).
+ */
+int rb_rep_gather_ln_quant(const void* table, int table_dtype, int64_t num_rows, int emb_dim,
+                           const int64_t* const* slot_values, const int64_t* const* slot_offsets,
+                           const int64_t* slot_nnz, int num_slots, int64_t num_items,
+                           const void* ln_gamma, const void* ln_beta, int ln_dtype, float eps,
+                           int act_mode, const void* static_scale, int static_scale_dtype,
+                           int8_t* q_out, int64_t ldq, float* scale_out, void* pooled_out,
+                           void* ln_out, void* stream);
+
+/*
+ * Gather + sum-pool only (models.py:27-34, the 28 nn.EmbeddingBag calls), for
+ * a subset of slots, writing pooled rows [num_items, ldp] (row dtype = table
+ * dtype) with slot j of the call at columns [col_slot[j]*512, +512).  Used by
+ * the slot-sharded multi-GPU path before the pooled-row exchange.
+ */
+int rb_rep_gather_pool(const void* table, int table_dtype, int64_t num_rows, int emb_dim,
+                       const int64_t* const* slot_values, const int64_t* const* slot_offsets,
+                       const int64_t* slot_nnz, const int* col_slot, int num_slots,
+                       int64_t num_items, void* pooled_out, int64_t ldp, void* stream);
+
+/*
+ * LayerNorm + int8 quantisation of dense pooled rows x[num_items, ldx]
+ * (x_dtype, width num_slots*512): the part of rb_rep_gather_ln_quant after the
+ * gather (models.py:45 + w8a8_triton_kernels.py:392-460), with the same
+ * arithmetic.  RB_ACT_NONE writes only ln_out (kernels/rep_encoder_fusion.py:6-30
+ * LayerNorm for the unquantised LN+Linear path).
+ */
+int rb_layernorm_quant(const void* x, int x_dtype, int64_t num_items, int num_slots, int64_t ldx,
+                       const void* ln_gamma, const void* ln_beta, int ln_dtype, float eps,
+                       int act_mode, const void* static_scale, int static_scale_dtype,
+                       int8_t* q_out, int64_t ldq, float* scale_out, void* ln_out, void* stream);
+
+/* quantization/w8a8_triton_kernels.py:41-64,392-422 dynamic_per_token_quantize_activation[_out]:
+ * x[M,K] (row stride ldx elements) -> q[M,K] (row stride ldq), scale[M] fp32. */
+int rb_quant_dynamic_per_token(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                               int8_t* q, int64_t ldq, float* scale, void* stream);
+
+/* quantization/w8a8_triton_kernels.py:23-38,375-389 static_quantize_activation[_out]:
+ * contiguous x[numel] with per-tensor scale[0] (scale_dtype RB_F32/RB_BF16/RB_F16). */
+int rb_quant_static(const void* x, int x_dtype, int64_t numel, const void* scale, int scale_dtype,
+                    int8_t* q, void* stream);
+
+/* kernels/quantization.py:6-35,243-278 quantize_rows_int8_triton (v1 rounding):
+ * x[M,K] -> q[M,K] in [-127,127], scale[M] = max(amax/127, 1e-8). */
+int rb_quant_rows_v1(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int8_t* q,
+                     int64_t ldq, float* scale, void* stream);
+
+/* quantization/w8a8_preprocess.py:46-57 quantize_weight_per_channel:
+ * w[N,K] (w_dtype, row stride ldw) -> q[N,K] int8 (round half to even) and scale[N] fp32. */
+int rb_quantize_weight_per_channel(const void* w, int w_dtype, int64_t N, int64_t K, int64_t ldw,
+                                   int8_t* q, float* scale, void* stream);
+
+/* Repack a [K,N] int8 weight view with element strides (stride_k, stride_n) into
+ * the GEMM's K-contiguous [N,K] layout (quantization_utils.py:21 stores qweight_t
+ * row-major [K,N]; w8a8_preprocess.py:54 makes it a transposed view). */
+int rb_pack_weight_nk(const int8_t* src, int64_t K, int64_t N, int64_t stride_k, int64_t stride_n,
+                      int8_t* dst, void* stream);
+
+/*
+ * W8A8 GEMM: acc[m,n] = sum_k A[m,k] * B[n,k] (int32, exact), then
+ *   out = ((f32(acc) * sa) * sb[n]) + bias[n]      stored as out_dtype
+ * or the raw int32 acc when out_dtype == RB_I32 (scales/bias ignored).
+ * Replaces quantization/w8a8_triton_kernels.py:174-318,470-640
+ * (w8a8_scaled_mm[_out], int8_mm_no_scale[_out]) and kernels/quantization.py:38-105
+ * (_w8a8_matmul_kernel).  tcgen05 kind::i8 on sm_100a with the accumulator in TMEM.
+ *   A     int8 [M, lda]  (K contiguous; lda % 16 == 0, 16-byte aligned)
+ *   B     int8 [N, ldb]  (K contiguous; ldb % 16 == 0, 16-byte aligned)
+ *   sa    per-row [M] (sa_per_row=1) or scalar [1]; sa_dtype RB_F32/RB_BF16/RB_F16
+ *   sb    [N], sb_dtype; bias [N] bias_dtype or NULL
+ *   out   [M, ldo] out_dtype RB_BF16 / RB_F16 / RB_F32 / RB_I32
+ */
+int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M, int64_t N,
+                 int64_t K, const void* sa, int sa_dtype, int sa_per_row, const void* sb,
+                 int sb_dtype, const void* bias, int bias_dtype, void* out, int64_t ldo,
+                 int out_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* REP_B200_H */

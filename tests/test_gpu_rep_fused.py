@@ -1,0 +1,197 @@
+"""K1 (fused gather -> pool -> LayerNorm -> int8) on the GPU against the oracle.
+
+Bit-exact: pooled rows, LayerNorm rows, int8 activations and per-token scales
+(the oracle restates the reference's arithmetic with the canonical LayerNorm
+reduction order).  Against the reference's own outputs (golden fixtures made
+by the reference's RepEncoder + Triton quantiser): pooled rows bit-exact, int8
+within one step on at most a few elements (ATen's LayerNorm reduces in a
+different order).
+"""
+
+import numpy as np
+import pytest
+
+from conftest import golden_rep
+
+pytestmark = pytest.mark.gpu
+
+
+def _to_dev_batch(torch, batch, dev, slots=28):
+    vals = [torch.from_numpy(np.ascontiguousarray(batch[s][0])).to(dev) for s in range(1, slots + 1)]
+    offs = [torch.from_numpy(np.ascontiguousarray(batch[s][1])).to(dev) for s in range(1, slots + 1)]
+    return vals, offs
+
+
+def _table_tensor(torch, table_np, dt, dev):
+    if dt == "bfloat16":
+        return torch.from_numpy(table_np.view(np.int16)).view(torch.bfloat16).to(dev)
+    return torch.from_numpy(table_np).to(dev)
+
+
+def _row_f32(torch, t):
+    return t.float().cpu().numpy()
+
+
+def _run_k1(torch, table, vals, offs, gamma, beta, eps, act_mode="dynamic", static_scale=None):
+    from baidu_cti_grab_b200 import device_ops
+
+    return device_ops.rep_gather_ln_quant(table, vals, offs, gamma, beta, eps, act_mode=act_mode,
+                                          static_scale=static_scale, want_pooled=True, want_ln=True)
+
+
+@pytest.mark.parametrize("fixture", ["rep_bf16.npz", "rep_f32.npz"])
+def test_k1_golden_bit_exact(cuda_device, fixture):
+    import torch
+    from oracle import oracle as O
+
+    dt, table_np, batch, gamma, beta, eps, z = golden_rep(fixture)
+    tdt = torch.bfloat16 if dt == "bfloat16" else torch.float32
+    table = _table_tensor(torch, table_np, dt, cuda_device)
+    vals, offs = _to_dev_batch(torch, batch, cuda_device)
+    g = torch.from_numpy(gamma).to(cuda_device, tdt)
+    b = torch.from_numpy(beta).to(cuda_device, tdt)
+    q, scale, pooled, ln = _run_k1(torch, table, vals, offs, g, b, eps)
+    torch.cuda.synchronize()
+    oq, oscale, opooled, oln = O.rep_forward(table_np, dt, batch, gamma, beta, eps, intermediates=True)
+    assert np.array_equal(_row_f32(torch, pooled), opooled)
+    assert np.array_equal(_row_f32(torch, ln), oln)
+    assert np.array_equal(q.cpu().numpy(), oq)
+    assert np.array_equal(scale.cpu().numpy(), oscale)
+    # the reference itself: pooled rows exact, int8 within one step on a few elements
+    tof = O.bf16_bits_to_f32 if dt == "bfloat16" else (lambda a: a.astype(np.float32))
+    assert np.array_equal(_row_f32(torch, pooled), tof(z["pooled_ref"]))
+    dq = np.abs(q.cpu().numpy().astype(np.int32) - z["q_dyn_ref"].astype(np.int32))
+    assert dq.max() <= 1
+    assert (dq != 0).mean() <= 1e-3
+
+
+def test_k1_static_mode(cuda_device):
+    import torch
+    from oracle import oracle as O
+
+    dt, table_np, batch, gamma, beta, eps, z = golden_rep("rep_bf16.npz")
+    table = _table_tensor(torch, table_np, dt, cuda_device)
+    vals, offs = _to_dev_batch(torch, batch, cuda_device)
+    g = torch.from_numpy(gamma).to(cuda_device, torch.bfloat16)
+    b = torch.from_numpy(beta).to(cuda_device, torch.bfloat16)
+    for sdt in (torch.float32, torch.bfloat16):
+        s = torch.from_numpy(z["static_scale"]).to(cuda_device, sdt)
+        q, scale, _, _ = _run_k1(torch, table, vals, offs, g, b, eps, act_mode="static", static_scale=s)
+        assert scale is None
+        oq, _ = O.rep_forward(table_np, dt, batch, gamma, beta, eps, act_mode="static",
+                              static_scale=float(s.float().item()))
+        assert np.array_equal(q.cpu().numpy(), oq)
+
+
+@pytest.mark.parametrize("dt,seed,users", [("bfloat16", 11, 48), ("float32", 12, 16)])
+def test_k1_synthetic_bit_exact(cuda_device, dt, seed, users):
+    import torch
+    from oracle import oracle as O
+    from baidu_cti_grab_b200 import synth
+
+    cfg = synth.WorkloadConfig("test", 500, dt, users, 1, 60, "1+poisson1", 1.1)
+    batch = synth.make_batch(cfg, seed=seed)
+    table_np = synth.make_table_numpy(cfg.num_rows, seed=seed, dtype=dt)
+    rng = np.random.default_rng(seed)
+    gamma = (1.0 + 0.2 * rng.standard_normal(28 * 512)).astype(np.float32)
+    beta = (0.05 * rng.standard_normal(28 * 512)).astype(np.float32)
+    tdt = torch.bfloat16 if dt == "bfloat16" else torch.float32
+    gamma = O.round_to(gamma, dt)
+    beta = O.round_to(beta, dt)
+    table = _table_tensor(torch, table_np, dt, cuda_device)
+    vals, offs = _to_dev_batch(torch, batch, cuda_device)
+    q, scale, pooled, ln = _run_k1(torch, table, vals, offs, torch.from_numpy(gamma).to(cuda_device, tdt),
+                                   torch.from_numpy(beta).to(cuda_device, tdt), 1e-5)
+    oq, oscale, opooled, oln = O.rep_forward(table_np, dt, batch, gamma, beta, 1e-5, intermediates=True)
+    assert np.array_equal(_row_f32(torch, pooled), opooled)
+    assert np.array_equal(_row_f32(torch, ln), oln)
+    assert np.array_equal(q.cpu().numpy(), oq)
+    assert np.array_equal(scale.cpu().numpy(), oscale)
+
+
+def test_k1_fp32_affine_params_on_bf16_rows(cuda_device):
+    """LayerNorm gamma/beta kept in fp32 while the table is bf16 (mixed module dtypes)."""
+    import torch
+    from oracle import oracle as O
+
+    dt, table_np, batch, gamma, beta, eps, _ = golden_rep("rep_bf16.npz")
+    table = _table_tensor(torch, table_np, dt, cuda_device)
+    vals, offs = _to_dev_batch(torch, batch, cuda_device)
+    rng = np.random.default_rng(5)
+    g32 = (1.0 + 0.3 * rng.standard_normal(28 * 512)).astype(np.float32)
+    b32 = (0.1 * rng.standard_normal(28 * 512)).astype(np.float32)
+    q, scale, _, ln = _run_k1(torch, table, vals, offs, torch.from_numpy(g32).to(cuda_device),
+                              torch.from_numpy(b32).to(cuda_device), eps)
+    oq, oscale, _, oln = O.rep_forward(table_np, dt, batch, g32, b32, eps, intermediates=True)
+    assert np.array_equal(_row_f32(torch, ln), oln)
+    assert np.array_equal(q.cpu().numpy(), oq)
+    assert np.array_equal(scale.cpu().numpy(), oscale)
+
+
+def test_k1_edge_cases(cuda_device):
+    """Zero items, one item, every bag empty, ids out of range / negative / padding."""
+    import torch
+    from oracle import oracle as O
+    from baidu_cti_grab_b200 import device_ops
+
+    dev = cuda_device
+    V = 40
+    table_np = (np.random.default_rng(0).standard_normal((V, 512)) * 0.02).astype(np.float32)
+    table = torch.from_numpy(table_np).to(dev)
+    g = torch.ones(28 * 512, device=dev)
+    b = torch.zeros(28 * 512, device=dev)
+    # zero items
+    vals = [torch.zeros(0, dtype=torch.int64, device=dev) for _ in range(28)]
+    offs = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(28)]
+    q, s, _, _ = device_ops.rep_gather_ln_quant(table, vals, offs, g, b, 1e-5)
+    assert q.shape == (0, 28 * 512)
+    # three items: all bags empty for item 0, item 1 has odd ids, item 2 long bags
+    batch = {"user_offsets": np.array([0, 3])}
+    rng = np.random.default_rng(1)
+    for sl in range(1, 29):
+        ids = np.concatenate([np.array([0, -7, V + 5, 3], dtype=np.int64), rng.integers(1, V, 40)])
+        batch[sl] = (ids, np.array([0, 0, 4, 44], dtype=np.int64))
+    vals, offs = _to_dev_batch(torch, batch, dev)
+    q, s, pooled, ln = device_ops.rep_gather_ln_quant(table, vals, offs, g, b, 1e-5, want_pooled=True,
+                                                      want_ln=True)
+    oq, os_, opooled, oln = O.rep_forward(table_np, "float32", batch, np.ones(28 * 512, np.float32),
+                                          np.zeros(28 * 512, np.float32), 1e-5, intermediates=True)
+    assert np.array_equal(pooled.cpu().numpy(), opooled)
+    assert np.all(pooled[0].cpu().numpy() == 0)
+    assert np.array_equal(q.cpu().numpy(), oq)
+    assert np.array_equal(s.cpu().numpy(), os_)
+
+
+def test_dense_layernorm_quant_matches_fused(cuda_device):
+    """rb_layernorm_quant on pooled rows == the fused kernel's LayerNorm/int8 stage."""
+    import torch
+    from baidu_cti_grab_b200 import device_ops
+
+    dt, table_np, batch, gamma, beta, eps, _ = golden_rep("rep_bf16.npz")
+    table = _table_tensor(torch, table_np, dt, cuda_device)
+    vals, offs = _to_dev_batch(torch, batch, cuda_device)
+    g = torch.from_numpy(gamma).to(cuda_device, torch.bfloat16)
+    b = torch.from_numpy(beta).to(cuda_device, torch.bfloat16)
+    q, s, pooled, ln = _run_k1(torch, table, vals, offs, g, b, eps)
+    q2, s2, ln2 = device_ops.layernorm_quant(pooled, g, b, eps, want_ln=True)
+    assert torch.equal(q, q2) and torch.equal(s, s2) and torch.equal(ln, ln2)
+    _, _, ln3 = device_ops.layernorm_quant(pooled, g, b, eps, act_mode="none")
+    assert torch.equal(ln, ln3)
+
+
+def test_gather_pool_column_placement(cuda_device):
+    """rb_rep_gather_pool writes each slot's pooled row at its requested column block."""
+    import torch
+    from baidu_cti_grab_b200 import device_ops
+
+    dt, table_np, batch, gamma, beta, eps, _ = golden_rep("rep_bf16.npz")
+    table = _table_tensor(torch, table_np, dt, cuda_device)
+    vals, offs = _to_dev_batch(torch, batch, cuda_device)
+    _, _, pooled, _ = _run_k1(torch, table, vals, offs, torch.from_numpy(gamma).to(cuda_device, torch.bfloat16),
+                              torch.from_numpy(beta).to(cuda_device, torch.bfloat16), eps)
+    sel = [3, 7, 11, 27, 0]
+    out = device_ops.rep_gather_pool(table, [vals[s] for s in sel], [offs[s] for s in sel],
+                                     col_slot=list(range(len(sel)))[::-1], width_slots=len(sel))
+    for j, s in enumerate(sel):
+        c = len(sel) - 1 - j
+        assert torch.equal(out[:, c * 512:(c + 1) * 512], pooled[:, s * 512:(s + 1) * 512])
