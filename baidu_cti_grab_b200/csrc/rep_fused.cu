@@ -22,7 +22,7 @@ namespace rb {
 
 constexpr int kSlotsPerWarp = 4;
 constexpr int kDim = 512;
-constexpr int kRowsInFlight = 4;  // table rows a warp keeps in flight
+constexpr int kRowsInFlight = 2;  // table rows a warp holds in registers (the rest are prefetched to L2)
 
 enum RepMode : int { kGatherLnQuant = 0, kGatherPool = 1, kDenseLnQuant = 2 };
 
@@ -56,118 +56,67 @@ struct RepParams {
   void* ln;
 };
 
-// 16 values of one slot held by one lane, in the row dtype.
-template <typename T>
-struct Frag;
-
-template <>
-struct Frag<__nv_bfloat16> {
-  uint32_t w[8];  // w[0..3]: cols 8l..8l+7, w[4..7]: cols 256+8l..256+8l+7 (lo half first)
-  __device__ __forceinline__ float get(int e) const {
-    uint32_t v = w[e >> 1];
-    return (e & 1) ? bf16_hi(v) : bf16_lo(v);
-  }
-  // store fp32 values rounded to bf16 (RNE)
-  __device__ __forceinline__ void set_pair(int p, float lo, float hi) { w[p] = pack_bf16x2(lo, hi); }
-  __device__ __forceinline__ void load(const void* row_base, int lane) {
-    const uint4* p = reinterpret_cast<const uint4*>(row_base);
-    uint4 a = p[lane], b = p[32 + lane];
-    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
-    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
-  }
-  __device__ __forceinline__ void store(void* row_base, int lane) const {
-    uint4* p = reinterpret_cast<uint4*>(row_base);
-    p[lane] = make_uint4(w[0], w[1], w[2], w[3]);
-    p[32 + lane] = make_uint4(w[4], w[5], w[6], w[7]);
-  }
+// ------------------------------------------------------------ f32x2 math
+// Blackwell packed fp32: one instruction performs two IEEE round-to-nearest
+// operations.  Lanes of a pair are independent, so results equal the scalar ops.
+struct F2 {
+  unsigned long long r;
 };
+__device__ __forceinline__ F2 f2(float lo, float hi) {
+  F2 v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v.r) : "f"(lo), "f"(hi));
+  return v;
+}
+__device__ __forceinline__ float2 un(F2 v) {
+  float2 o;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(v.r));
+  return o;
+}
+__device__ __forceinline__ F2 add2(F2 a, F2 b) {
+  F2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
+  return d;
+}
+__device__ __forceinline__ F2 sub2(F2 a, F2 b) {
+  F2 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
+  return d;
+}
+__device__ __forceinline__ F2 mul2(F2 a, F2 b) {
+  F2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
+  return d;
+}
+__device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) {
+  F2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.r) : "l"(a.r), "l"(b.r), "l"(c.r));
+  return d;
+}
+__device__ __forceinline__ F2 addrz2(F2 a, F2 b) {
+  F2 d;
+  asm("add.rz.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
+  return d;
+}
+// bf16 pair packed in a 32-bit word (lo element in the low half) -> fp32 pair
+__device__ __forceinline__ F2 bf2(uint32_t w) { return f2(bf16_lo(w), bf16_hi(w)); }
 
-template <>
-struct Frag<float> {
-  float f[16];
-  __device__ __forceinline__ float get(int e) const { return f[e]; }
-  __device__ __forceinline__ void set_pair(int p, float lo, float hi) {
-    f[2 * p] = lo;
-    f[2 * p + 1] = hi;
-  }
-  __device__ __forceinline__ void load(const void* row_base, int lane) {
-    const float4* p = reinterpret_cast<const float4*>(row_base);
-    float4 a = p[2 * lane], b = p[2 * lane + 1], c = p[64 + 2 * lane], d = p[64 + 2 * lane + 1];
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-    f[8] = c.x; f[9] = c.y; f[10] = c.z; f[11] = c.w; f[12] = d.x; f[13] = d.y; f[14] = d.z; f[15] = d.w;
-  }
-  __device__ __forceinline__ void store(void* row_base, int lane) const {
-    float4* p = reinterpret_cast<float4*>(row_base);
-    p[2 * lane] = make_float4(f[0], f[1], f[2], f[3]);
-    p[2 * lane + 1] = make_float4(f[4], f[5], f[6], f[7]);
-    p[64 + 2 * lane] = make_float4(f[8], f[9], f[10], f[11]);
-    p[64 + 2 * lane + 1] = make_float4(f[12], f[13], f[14], f[15]);
-  }
-};
+// round_half_away_from_zero(v) for |v| < 2^23, exactly: the result is
+// trunc(v + copysign(0.5, v)) with the addition rounded toward zero, because
+// floor(RZ(|v| + 0.5)) == floor(|v| + 0.5) (every integer below 2^24 is
+// representable, and rounding toward zero never crosses one downward).
+__device__ __forceinline__ void round_half_away2(F2 v, int& q0, int& q1) {
+  const float2 x = un(v);
+  const F2 h = f2(__uint_as_float((__float_as_uint(x.x) & 0x80000000u) | 0x3f000000u),
+                  __uint_as_float((__float_as_uint(x.y) & 0x80000000u) | 0x3f000000u));
+  const float2 r = un(addrz2(v, h));
+  q0 = __float2int_rz(r.x);
+  q1 = __float2int_rz(r.y);
+}
 
-// Raw table row piece of one lane (same column ownership as Frag).
-template <typename T>
-struct RowBuf;
-
-template <>
-struct RowBuf<__nv_bfloat16> {
-  uint4 a, b;
-  __device__ __forceinline__ void load(const __nv_bfloat16* row, int lane) {
-    const uint4* p = reinterpret_cast<const uint4*>(row);
-    a = __ldg(p + lane);
-    b = __ldg(p + 32 + lane);
-  }
-  __device__ __forceinline__ void add_to(float* acc) const {
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      acc[2 * i] = __fadd_rn(acc[2 * i], bf16_lo(w[i]));
-      acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], bf16_hi(w[i]));
-    }
-  }
-};
-
-template <>
-struct RowBuf<float> {
-  float4 a, b, c, d;
-  __device__ __forceinline__ void load(const float* row, int lane) {
-    const float4* p = reinterpret_cast<const float4*>(row);
-    a = __ldg(p + 2 * lane);
-    b = __ldg(p + 2 * lane + 1);
-    c = __ldg(p + 64 + 2 * lane);
-    d = __ldg(p + 64 + 2 * lane + 1);
-  }
-  __device__ __forceinline__ void add_to(float* acc) const {
-    const float v[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w,
-                         c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
-#pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = __fadd_rn(acc[i], v[i]);
-  }
-};
-
-// 8 consecutive LayerNorm affine parameters, widened to fp32.
-__device__ __forceinline__ void load8_f32(const void* p, int dtype, int64_t idx, float* out) {
-  if (dtype == RB_F32) {
-    const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + idx);
-    float4 a = __ldg(q), b = __ldg(q + 1);
-    out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
-    out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
-  } else {
-    uint4 v = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + idx));
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (dtype == RB_BF16) {
-        out[2 * i] = bf16_lo(w[i]);
-        out[2 * i + 1] = bf16_hi(w[i]);
-      } else {
-        __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
-        float2 f = __half22float2(h);
-        out[2 * i] = f.x;
-        out[2 * i + 1] = f.y;
-      }
-    }
-  }
+__device__ __forceinline__ uint32_t pack_i8x4_prmt(int a, int b, int c, int d) {
+  const uint32_t ab = __byte_perm((uint32_t)a, (uint32_t)b, 0x0040);
+  const uint32_t cd = __byte_perm((uint32_t)c, (uint32_t)d, 0x0040);
+  return __byte_perm(ab, cd, 0x5410);
 }
 
 __device__ __forceinline__ float warp_sum_butterfly(float v) {
@@ -182,9 +131,152 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// a[j] for a runtime j in [0, 4) without dynamic register indexing
-__device__ __forceinline__ int64_t sel4(const int64_t* a, int j) {
-  return j == 0 ? a[0] : (j == 1 ? a[1] : (j == 2 ? a[2] : a[3]));
+// ------------------------------------------------ row layout per element type
+// A lane's 16 values of a 512-wide slot segment: columns 8l..8l+7 then
+// 256+8l..256+8l+7, held as 8 fp32 pairs (pair p = elements 2p, 2p+1).
+template <typename T>
+struct Seg;
+
+template <>
+struct Seg<__nv_bfloat16> {
+  static constexpr int kBytes = 2;
+  // load 16 values of a bf16 row segment (global or shared) as 8 words
+  __device__ __forceinline__ static void load_words(const __nv_bfloat16* base, int lane, uint32_t* w) {
+    const uint4* p = reinterpret_cast<const uint4*>(base);
+    const uint4 a = p[lane], b = p[32 + lane];
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+  }
+  __device__ __forceinline__ static void load_pairs(const __nv_bfloat16* base, int lane, F2* x) {
+    uint32_t w[8];
+    load_words(base, lane, w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = bf2(w[i]);
+  }
+  // round 8 fp32 pairs to bf16 (RNE) and store; returns the rounded pairs in x
+  __device__ __forceinline__ static void round_store(__nv_bfloat16* base, int lane, F2* x) {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float2 v = un(x[i]);
+      w[i] = pack_bf16x2(v.x, v.y);
+      x[i] = bf2(w[i]);
+    }
+    uint4* p = reinterpret_cast<uint4*>(base);
+    p[lane] = make_uint4(w[0], w[1], w[2], w[3]);
+    p[32 + lane] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+};
+
+template <>
+struct Seg<float> {
+  static constexpr int kBytes = 4;
+  __device__ __forceinline__ static void load_pairs(const float* base, int lane, F2* x) {
+    const float4* p = reinterpret_cast<const float4*>(base);
+    const float4 a = p[2 * lane], b = p[2 * lane + 1], c = p[64 + 2 * lane], d = p[64 + 2 * lane + 1];
+    x[0] = f2(a.x, a.y); x[1] = f2(a.z, a.w); x[2] = f2(b.x, b.y); x[3] = f2(b.z, b.w);
+    x[4] = f2(c.x, c.y); x[5] = f2(c.z, c.w); x[6] = f2(d.x, d.y); x[7] = f2(d.z, d.w);
+  }
+  __device__ __forceinline__ static void round_store(float* base, int lane, F2* x) {
+    float4* p = reinterpret_cast<float4*>(base);
+    const float2 v0 = un(x[0]), v1 = un(x[1]), v2 = un(x[2]), v3 = un(x[3]);
+    const float2 v4 = un(x[4]), v5 = un(x[5]), v6 = un(x[6]), v7 = un(x[7]);
+    p[2 * lane] = make_float4(v0.x, v0.y, v1.x, v1.y);
+    p[2 * lane + 1] = make_float4(v2.x, v2.y, v3.x, v3.y);
+    p[64 + 2 * lane] = make_float4(v4.x, v4.y, v5.x, v5.y);
+    p[64 + 2 * lane + 1] = make_float4(v6.x, v6.y, v7.x, v7.y);
+  }
+};
+
+// One table row piece of a lane, loaded ahead of its accumulation.
+template <typename T>
+struct RowBuf;
+
+template <>
+struct RowBuf<__nv_bfloat16> {
+  uint4 a, b;
+  __device__ __forceinline__ void load(const __nv_bfloat16* row, int lane) {
+    const uint4* p = reinterpret_cast<const uint4*>(row);
+    a = __ldg(p + lane);
+    b = __ldg(p + 32 + lane);
+  }
+  __device__ __forceinline__ void add_to(F2* acc) const {
+    acc[0] = add2(acc[0], bf2(a.x)); acc[1] = add2(acc[1], bf2(a.y));
+    acc[2] = add2(acc[2], bf2(a.z)); acc[3] = add2(acc[3], bf2(a.w));
+    acc[4] = add2(acc[4], bf2(b.x)); acc[5] = add2(acc[5], bf2(b.y));
+    acc[6] = add2(acc[6], bf2(b.z)); acc[7] = add2(acc[7], bf2(b.w));
+  }
+};
+
+template <>
+struct RowBuf<float> {
+  float4 a, b, c, d;
+  __device__ __forceinline__ void load(const float* row, int lane) {
+    const float4* p = reinterpret_cast<const float4*>(row);
+    a = __ldg(p + 2 * lane);
+    b = __ldg(p + 2 * lane + 1);
+    c = __ldg(p + 64 + 2 * lane);
+    d = __ldg(p + 64 + 2 * lane + 1);
+  }
+  __device__ __forceinline__ void add_to(F2* acc) const {
+    acc[0] = add2(acc[0], f2(a.x, a.y)); acc[1] = add2(acc[1], f2(a.z, a.w));
+    acc[2] = add2(acc[2], f2(b.x, b.y)); acc[3] = add2(acc[3], f2(b.z, b.w));
+    acc[4] = add2(acc[4], f2(c.x, c.y)); acc[5] = add2(acc[5], f2(c.z, c.w));
+    acc[6] = add2(acc[6], f2(d.x, d.y)); acc[7] = add2(acc[7], f2(d.z, d.w));
+  }
+};
+
+// 16 LayerNorm affine parameters of a lane's columns as fp32 pairs (fp32 input)
+__device__ __forceinline__ void load_affine_f32(const float* p, int64_t col0, F2* out) {
+  const float4* q = reinterpret_cast<const float4*>(p + col0);
+  const float4 a = __ldg(q), b = __ldg(q + 1), c = __ldg(q + 64), d = __ldg(q + 65);
+  out[0] = f2(a.x, a.y); out[1] = f2(a.z, a.w); out[2] = f2(b.x, b.y); out[3] = f2(b.z, b.w);
+  out[4] = f2(c.x, c.y); out[5] = f2(c.z, c.w); out[6] = f2(d.x, d.y); out[7] = f2(d.z, d.w);
+}
+
+// same for 16-bit (bf16 / fp16) parameters
+__device__ __forceinline__ void load_affine(const void* p, int dtype, int64_t col0, F2* out) {
+  if (dtype == RB_F32) {
+    load_affine_f32(reinterpret_cast<const float*>(p), col0, out);
+    return;
+  }
+  const uint4* q = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + col0);
+  const uint4 a = __ldg(q), c = __ldg(q + 32);
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (dtype == RB_BF16) {
+      out[i] = bf2(w[i]);
+    } else {
+      const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      out[i] = f2(h.x, h.y);
+    }
+  }
+}
+
+// canonical lane partial of 8 pairs: even positions in .x, odd in .y, then x + y
+__device__ __forceinline__ float lane_partial(const F2* x) {
+  F2 a = f2(0.0f, 0.0f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a = add2(a, x[i]);
+  const float2 v = un(a);
+  return __fadd_rn(v.x, v.y);
+}
+
+__device__ __forceinline__ float lane_partial_sq(const F2* x, F2 mean2) {
+  F2 a = f2(0.0f, 0.0f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const F2 d = sub2(x[i], mean2);
+    a = fma2(d, d, a);
+  }
+  const float2 v = un(a);
+  return __fadd_rn(v.x, v.y);
+}
+
+// Ask the copy engine to bring `bytes` at `p` into L2 (no registers, no wait).
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ int64_t shfl_i64(int64_t v, int src) {
@@ -193,8 +285,22 @@ __device__ __forceinline__ int64_t shfl_i64(int64_t v, int src) {
   return ((int64_t)hi << 32) | (uint32_t)lo;
 }
 
+// a[j] for a runtime j in [0, 4) without dynamic register indexing
+template <typename V>
+__device__ __forceinline__ V sel4(const V* a, int j) {
+  return j == 0 ? a[0] : (j == 1 ? a[1] : (j == 2 ? a[2] : a[3]));
+}
+
+// One CTA per item.  Warp w owns slots 4w..4w+3: it gathers their bags with
+// kRowsInFlight rows in flight, rounds each bag sum to the row dtype into the
+// shared-memory row (S*512 values) and contributes the slot's first-pass
+// LayerNorm partial.  The remaining passes read the row back from shared
+// memory: variance, normalise + affine (written back in place) with the
+// absmax, then the int8 quantiser.  gamma/beta arrive as fp32.
 template <typename T, int MODE>
-__global__ void __launch_bounds__(256, 2) rep_fused_kernel(const __grid_constant__ RepParams p) {
+__global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant__ RepParams p) {
+  extern __shared__ __align__(16) uint8_t s_row_raw[];
+  T* s_row = reinterpret_cast<T*>(s_row_raw);
   __shared__ float s_tot[RB_MAX_SLOTS];
   __shared__ float s_wmax[8];
   __shared__ float s_stat[4];  // mean, rstd, scale, inv
@@ -206,13 +312,16 @@ __global__ void __launch_bounds__(256, 2) rep_fused_kernel(const __grid_constant
   const int slot0 = warp * kSlotsPerWarp;
   const int nsl = max(0, min(kSlotsPerWarp, S - slot0));
 
-  Frag<T> frag[kSlotsPerWarp];
-
   if constexpr (MODE == kDenseLnQuant) {
     const T* xrow = reinterpret_cast<const T*>(p.x) + item * p.ldx;
-#pragma unroll
-    for (int j = 0; j < kSlotsPerWarp; ++j)
-      if (j < nsl) frag[j].load(xrow + (int64_t)(slot0 + j) * kDim, lane);
+    for (int j = 0; j < nsl; ++j) {
+      const int s = slot0 + j;
+      F2 x[8];
+      Seg<T>::load_pairs(xrow + (int64_t)s * kDim, lane, x);
+      Seg<T>::round_store(s_row + s * kDim, lane, x);  // identity rounding: values are already T
+      const float a = warp_sum_butterfly(lane_partial(x));
+      if (lane == 0) s_tot[s] = a;
+    }
   } else {
     // ---- bag bounds of this warp's slots: lanes 0-3 starts, lanes 4-7 ends
     int64_t bound = 0;
@@ -222,121 +331,84 @@ __global__ void __launch_bounds__(256, 2) rep_fused_kernel(const __grid_constant
         const int s = slot0 + j;
         const int64_t nz = p.slots.nnz[s];
         const int64_t* off = p.slots.offsets[s];
-        int64_t b;
-        if (lane < 4) {
-          b = off[item];
-        } else {
-          b = (item + 1 < p.num_items) ? off[item + 1] : nz;
-        }
+        const int64_t b = (lane < 4) ? off[item] : ((item + 1 < p.num_items) ? off[item + 1] : nz);
         bound = b < 0 ? 0 : (b > nz ? nz : b);
       }
     }
-    int64_t start[kSlotsPerWarp], cnt[kSlotsPerWarp];
-    int64_t total = 0, pre[kSlotsPerWarp + 1];
+    int64_t start[kSlotsPerWarp];
+    int pre[kSlotsPerWarp + 1];
+    int total = 0;
 #pragma unroll
     for (int j = 0; j < kSlotsPerWarp; ++j) {
       start[j] = shfl_i64(bound, j);
       const int64_t e = shfl_i64(bound, 4 + j);
-      cnt[j] = (j < nsl && e > start[j]) ? e - start[j] : 0;
       pre[j] = total;
-      total += cnt[j];
+      total += (j < nsl && e > start[j]) ? (int)(e - start[j]) : 0;
     }
     pre[kSlotsPerWarp] = total;
 
     const T* table = reinterpret_cast<const T*>(p.table);
-    const int64_t vmax = p.num_rows - 1;
-    float acc[16];
+    const int vmax = (int)(p.num_rows - 1);
+    F2 acc[8];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
+    for (int i = 0; i < 8; ++i) acc[i] = f2(0.0f, 0.0f);
     int cur = 0;  // slot (0..nsl) whose bag is being summed
 
     auto finish_slot = [&](int j) {
-      // round the fp32 bag sum to the row dtype (nn.EmbeddingBag output)
-#pragma unroll
-      for (int jj = 0; jj < kSlotsPerWarp; ++jj) {
-        if (jj == j) {
-#pragma unroll
-          for (int pr = 0; pr < 8; ++pr) frag[jj].set_pair(pr, acc[2 * pr], acc[2 * pr + 1]);
-        }
+      const int s = slot0 + j;
+      Seg<T>::round_store(s_row + s * kDim, lane, acc);  // nn.EmbeddingBag output dtype
+      const float a = warp_sum_butterfly(lane_partial(acc));
+      if (lane == 0) s_tot[s] = a;
+      if constexpr (MODE == kGatherPool) {
+        Seg<T>::round_store(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)p.slots.col_slot[s] * kDim,
+                            lane, acc);
+      } else {
+        if (p.pooled != nullptr)
+          Seg<T>::round_store(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, acc);
       }
 #pragma unroll
-      for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
+      for (int i = 0; i < 8; ++i) acc[i] = f2(0.0f, 0.0f);
     };
 
-    for (int64_t w0 = 0; w0 < total; w0 += 32) {
-      // ids of positions w0 .. w0+31 of the concatenated bag list
-      int64_t my_id = 0;
+    for (int w0 = 0; w0 < total; w0 += 32) {
+      // row ids of positions w0 .. w0+31 of the warp's concatenated bag list
+      int my_id = 0;
       {
-        const int64_t t = w0 + lane;
+        const int t = w0 + lane;
         if (t < total) {
           const int j = (t >= pre[1]) + (t >= pre[2]) + (t >= pre[3]);
           int64_t id = p.slots.values[slot0 + j][sel4(start, j) + (t - sel4(pre, j))];
-          id = id < 0 ? 0 : (id > vmax ? vmax : id);
-          my_id = id;
+          my_id = (int)(id < 0 ? 0 : (id > vmax ? vmax : id));
+          // every row of the window is requested at once; the register
+          // pipeline below then mostly hits L2
+          if (my_id != 0) prefetch_l2_bulk(table + (int64_t)my_id * kDim, kDim * Seg<T>::kBytes);
         }
       }
-      const int nwin = (total - w0 < 32) ? (int)(total - w0) : 32;
+      const int nwin = min(32, total - w0);
       for (int u0 = 0; u0 < nwin; u0 += kRowsInFlight) {
         RowBuf<T> buf[kRowsInFlight];
-        int64_t ids[kRowsInFlight];
+        int ids[kRowsInFlight];
 #pragma unroll
         for (int u = 0; u < kRowsInFlight; ++u) {
-          ids[u] = shfl_i64(my_id, (u0 + u) & 31);
-          if (u0 + u < nwin && ids[u] != 0) buf[u].load(table + ids[u] * kDim, lane);
+          ids[u] = __shfl_sync(0xffffffffu, my_id, (u0 + u) & 31);
+          if (u0 + u < nwin && ids[u] != 0) buf[u].load(table + (int64_t)ids[u] * kDim, lane);
         }
 #pragma unroll
         for (int u = 0; u < kRowsInFlight; ++u) {
           if (u0 + u < nwin) {
-            const int64_t t = w0 + u0 + u;
+            const int t = w0 + u0 + u;
             const int j = (t >= pre[1]) + (t >= pre[2]) + (t >= pre[3]);
-            while (cur < j) {
-              finish_slot(cur);
-              ++cur;
-            }
+            while (cur < j) finish_slot(cur++);
             if (ids[u] != 0) buf[u].add_to(acc);  // padding_idx 0 is excluded
           }
         }
       }
     }
-    while (cur < nsl) {
-      finish_slot(cur);
-      ++cur;
-    }
-
-    if constexpr (MODE == kGatherPool) {
-#pragma unroll
-      for (int j = 0; j < kSlotsPerWarp; ++j) {
-        if (j < nsl) {
-          T* dst = reinterpret_cast<T*>(p.pooled) + item * p.ldp +
-                   (int64_t)p.slots.col_slot[slot0 + j] * kDim;
-          frag[j].store(dst, lane);
-        }
-      }
-      return;
-    } else {
-      if (p.pooled != nullptr) {
-#pragma unroll
-        for (int j = 0; j < kSlotsPerWarp; ++j)
-          if (j < nsl)
-            frag[j].store(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)(slot0 + j) * kDim,
-                          lane);
-      }
-    }
+    while (cur < nsl) finish_slot(cur++);
   }
 
   if constexpr (MODE != kGatherPool) {
     const float H = (float)(S * kDim);
-    // ---- pass 1: mean
-#pragma unroll
-    for (int j = 0; j < kSlotsPerWarp; ++j) {
-      if (j < nsl) {
-        float a = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) a = __fadd_rn(a, frag[j].get(e));
-        a = warp_sum_butterfly(a);
-        if (lane == 0) s_tot[slot0 + j] = a;
-      }
-    }
     __syncthreads();
     if (threadIdx.x == 0) {
       float t = 0.0f;
@@ -345,19 +417,14 @@ __global__ void __launch_bounds__(256, 2) rep_fused_kernel(const __grid_constant
     }
     __syncthreads();
     const float mean = s_stat[0];
-    // ---- pass 2: variance (two-pass)
-#pragma unroll
-    for (int j = 0; j < kSlotsPerWarp; ++j) {
-      if (j < nsl) {
-        float a = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float d = __fsub_rn(frag[j].get(e), mean);
-          a = __fmaf_rn(d, d, a);
-        }
-        a = warp_sum_butterfly(a);
-        if (lane == 0) s_tot[slot0 + j] = a;
-      }
+    const F2 mean2 = f2(mean, mean);
+    // ---- pass 2: variance around the mean
+    for (int j = 0; j < nsl; ++j) {
+      const int s = slot0 + j;
+      F2 x[8];
+      Seg<T>::load_pairs(s_row + s * kDim, lane, x);
+      const float a = warp_sum_butterfly(lane_partial_sq(x, mean2));
+      if (lane == 0) s_tot[s] = a;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -368,30 +435,25 @@ __global__ void __launch_bounds__(256, 2) rep_fused_kernel(const __grid_constant
     }
     __syncthreads();
     const float rstd = s_stat[1];
-    // ---- pass 3: normalise + affine, round to the row dtype, absmax
+    const F2 rstd2 = f2(rstd, rstd);
+    // ---- pass 3: y = fma(rstd * (x - mean), gamma, beta), rounded to T, in place; absmax
     float amax = 0.0f;
+    for (int j = 0; j < nsl; ++j) {
+      const int s = slot0 + j;
+      F2 x[8], g[8], b[8];
+      Seg<T>::load_pairs(s_row + s * kDim, lane, x);
+      const int64_t col0 = (int64_t)s * kDim + 8 * lane;
+      load_affine(p.gamma, p.ln_dtype, col0, g);
+      load_affine(p.beta, p.ln_dtype, col0, b);
 #pragma unroll
-    for (int j = 0; j < kSlotsPerWarp; ++j) {
-      if (j < nsl) {
-        const int64_t col0 = (int64_t)(slot0 + j) * kDim + 8 * lane;
-        float g[16], b[16];
-        load8_f32(p.gamma, p.ln_dtype, col0, g);
-        load8_f32(p.gamma, p.ln_dtype, col0 + 256, g + 8);
-        load8_f32(p.beta, p.ln_dtype, col0, b);
-        load8_f32(p.beta, p.ln_dtype, col0 + 256, b + 8);
+      for (int i = 0; i < 8; ++i) x[i] = fma2(mul2(rstd2, sub2(x[i], mean2)), g[i], b[i]);
+      Seg<T>::round_store(s_row + s * kDim, lane, x);
 #pragma unroll
-        for (int pr = 0; pr < 8; ++pr) {
-          float y0 = __fmaf_rn(__fmul_rn(rstd, __fsub_rn(frag[j].get(2 * pr), mean)), g[2 * pr], b[2 * pr]);
-          float y1 = __fmaf_rn(__fmul_rn(rstd, __fsub_rn(frag[j].get(2 * pr + 1), mean)), g[2 * pr + 1],
-                               b[2 * pr + 1]);
-          frag[j].set_pair(pr, y0, y1);
-        }
-#pragma unroll
-        for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(frag[j].get(e)));
-        if (p.ln != nullptr)
-          frag[j].store(reinterpret_cast<T*>(p.ln) + item * (int64_t)(S * kDim) + (int64_t)(slot0 + j) * kDim,
-                        lane);
+      for (int i = 0; i < 8; ++i) {
+        const float2 v = un(x[i]);
+        amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
       }
+      if (p.ln != nullptr) Seg<T>::round_store(reinterpret_cast<T*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, x);
     }
     if (p.act_mode == RB_ACT_NONE) return;
     amax = warp_max(amax);
@@ -403,9 +465,9 @@ __global__ void __launch_bounds__(256, 2) rep_fused_kernel(const __grid_constant
         float m = 0.0f;
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, s_wmax[w]);
         m = fmaxf(m, 1e-8f);
-        s_stat[2] = __fdiv_rn(m, 127.0f);
+        const float sc = __fdiv_rn(m, 127.0f);
         inv = __fdiv_rn(127.0f, m);
-        p.scale[item] = s_stat[2];
+        p.scale[item] = sc;
       } else {
         inv = __fdiv_rn(1.0f, load_as_f32(p.static_scale, p.static_scale_dtype, 0));
       }
@@ -413,23 +475,29 @@ __global__ void __launch_bounds__(256, 2) rep_fused_kernel(const __grid_constant
     }
     __syncthreads();
     const float inv = s_stat[3];
-    // ---- pass 4: int8 = clamp(roundf(y * inv), -128, 127)
+    const F2 inv2 = f2(inv, inv);
+    const bool clamp = p.act_mode == RB_ACT_STATIC;
+    // ---- pass 4: int8 = clamp(round_half_away(y * inv), -128, 127)
+    for (int j = 0; j < nsl; ++j) {
+      const int s = slot0 + j;
+      F2 x[8];
+      Seg<T>::load_pairs(s_row + s * kDim, lane, x);
+      int q[16];
 #pragma unroll
-    for (int j = 0; j < kSlotsPerWarp; ++j) {
-      if (j < nsl) {
-        int qv[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float r = roundf(__fmul_rn(frag[j].get(e), inv));
-          r = fminf(fmaxf(r, -128.0f), 127.0f);
-          qv[e] = (int)r;
+      for (int i = 0; i < 8; ++i) {
+        F2 v = mul2(x[i], inv2);
+        if (clamp) {
+          // |y*inv| <= 127*(1+2^-23) in dynamic mode; a static scale needs the clamp
+          const float2 c = un(v);
+          v = f2(fminf(fmaxf(c.x, -128.0f), 127.0f), fminf(fmaxf(c.y, -128.0f), 127.0f));
         }
-        int8_t* dst = p.q + item * p.ldq + (int64_t)(slot0 + j) * kDim + 8 * lane;
-        *reinterpret_cast<uint2*>(dst) =
-            make_uint2(pack_i8x4(qv[0], qv[1], qv[2], qv[3]), pack_i8x4(qv[4], qv[5], qv[6], qv[7]));
-        *reinterpret_cast<uint2*>(dst + 256) = make_uint2(pack_i8x4(qv[8], qv[9], qv[10], qv[11]),
-                                                          pack_i8x4(qv[12], qv[13], qv[14], qv[15]));
+        round_half_away2(v, q[2 * i], q[2 * i + 1]);
       }
+      int8_t* dst = p.q + item * p.ldq + (int64_t)s * kDim + 8 * lane;
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack_i8x4_prmt(q[0], q[1], q[2], q[3]),
+                                                  pack_i8x4_prmt(q[4], q[5], q[6], q[7]));
+      *reinterpret_cast<uint2*>(dst + 256) = make_uint2(pack_i8x4_prmt(q[8], q[9], q[10], q[11]),
+                                                        pack_i8x4_prmt(q[12], q[13], q[14], q[15]));
     }
   }
 }
@@ -465,10 +533,19 @@ static int launch_rep(const RepParams& p, int row_dtype, cudaStream_t stream) {
   if (p.num_items == 0) return RB_OK;
   const int warps = (p.num_slots + kSlotsPerWarp - 1) / kSlotsPerWarp;
   dim3 grid((unsigned)p.num_items), block(32 * warps);
-  if (row_dtype == RB_BF16)
-    rep_fused_kernel<__nv_bfloat16, MODE><<<grid, block, 0, stream>>>(p);
-  else
-    rep_fused_kernel<float, MODE><<<grid, block, 0, stream>>>(p);
+  const size_t smem = (size_t)p.num_slots * kDim * dtype_size(row_dtype);
+  cudaError_t e = cudaSuccess;
+  if (row_dtype == RB_BF16) {
+    if (smem > 48 * 1024)
+      e = cudaFuncSetAttribute(rep_fused_kernel<__nv_bfloat16, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem);
+    if (e == cudaSuccess) rep_fused_kernel<__nv_bfloat16, MODE><<<grid, block, smem, stream>>>(p);
+  } else {
+    if (smem > 48 * 1024)
+      e = cudaFuncSetAttribute(rep_fused_kernel<float, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) rep_fused_kernel<float, MODE><<<grid, block, smem, stream>>>(p);
+  }
+  if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(rep_fused_kernel)");
   return check_cuda(cudaGetLastError(), "rep_fused_kernel launch");
 }
 
@@ -518,6 +595,7 @@ extern "C" int rb_rep_gather_ln_quant(const void* table, int table_dtype, int64_
   if (table == nullptr || !aligned(table, 16)) return fail(RB_ERR_VALUE, "table must be 16-byte aligned");
   if (num_rows < 1) return fail(RB_ERR_VALUE, "num_rows must be >= 1");
   if (slot_nnz == nullptr) return fail(RB_ERR_VALUE, "slot_nnz must be given");
+  if (num_items == 0) return RB_OK;  // empty batch: nothing to read or write
   rc = check_ln_args(ln_gamma, ln_beta, ln_dtype, act_mode, static_scale, static_scale_dtype, q_out, ldq,
                      scale_out, ln_out, num_slots);
   if (rc) return rc;
@@ -558,6 +636,7 @@ extern "C" int rb_rep_gather_pool(const void* table, int table_dtype, int64_t nu
   if (table == nullptr || !aligned(table, 16)) return fail(RB_ERR_VALUE, "table must be 16-byte aligned");
   if (num_rows < 1) return fail(RB_ERR_VALUE, "num_rows must be >= 1");
   if (slot_nnz == nullptr || col_slot == nullptr) return fail(RB_ERR_VALUE, "slot_nnz/col_slot must be given");
+  if (num_items == 0) return RB_OK;
   if (pooled_out == nullptr || !aligned(pooled_out, 16))
     return fail(RB_ERR_VALUE, "pooled_out must be 16-byte aligned");
   const int esz = dtype_size(table_dtype);
@@ -584,6 +663,7 @@ extern "C" int rb_layernorm_quant(const void* x, int x_dtype, int64_t num_items,
   int rc = validate_common(num_slots, num_items);
   if (rc) return rc;
   if (x_dtype != RB_BF16 && x_dtype != RB_F32) return fail(RB_ERR_VALUE, "x dtype must be RB_BF16 or RB_F32");
+  if (num_items == 0) return RB_OK;
   const int esz = dtype_size(x_dtype);
   if (x == nullptr || !aligned(x, 16) || (ldx * esz) % 16 != 0 || ldx < (int64_t)num_slots * kDim)
     return fail(RB_ERR_VALUE, "x must be 16-byte aligned with 16-byte row stride and ldx >= %d",

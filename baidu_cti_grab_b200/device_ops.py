@@ -9,6 +9,7 @@ rep_encoder_fusion, rep_encoder) are built on them.
 from __future__ import annotations
 
 import ctypes
+import weakref
 from typing import Optional, Sequence, Tuple
 
 import torch
@@ -56,6 +57,38 @@ def require_cuda(name: str, *tensors: Optional[torch.Tensor]) -> torch.device:
 
 
 # --------------------------------------------------------------- RepEncoder
+_DERIVED: dict = {}
+
+
+def cached_derived(src: torch.Tensor, tag: str, make):
+    """``make(src)`` computed once per (tensor object, tag) and reused while the
+    tensor is alive and unmodified (same storage pointer and version counter).
+    Entries die with their source tensor, so a new tensor that happens to
+    reuse a freed address never sees a stale value."""
+    key = (id(src), tag)
+    sig = (src.data_ptr(), src._version, src.dtype, tuple(src.shape), tuple(src.stride()), src.device)
+    hit = _DERIVED.get(key)
+    if hit is not None:
+        ref, hsig, value = hit
+        if ref() is src and hsig == sig:
+            return value
+    value = make(src)
+    try:
+        ref = weakref.ref(src, lambda _r, k=key: _DERIVED.pop(k, None))
+    except TypeError:
+        return value
+    _DERIVED[key] = (ref, sig, value)
+    return value
+
+
+def _affine_f32(t: torch.Tensor) -> torch.Tensor:
+    """fp32 copy of a LayerNorm parameter (exact widening); the kernel then
+    reads 4 values per load instead of unpacking 16-bit values."""
+    if t.dtype == torch.float32:
+        return t.contiguous()
+    return cached_derived(t, "affine_f32", lambda x: x.detach().float().contiguous())
+
+
 def rep_gather_ln_quant(table: torch.Tensor, slot_values: Sequence[torch.Tensor],
                         slot_offsets: Sequence[torch.Tensor], gamma: torch.Tensor, beta: torch.Tensor,
                         eps: float, act_mode: str = "dynamic", static_scale: Optional[torch.Tensor] = None,
@@ -87,8 +120,8 @@ def rep_gather_ln_quant(table: torch.Tensor, slot_values: Sequence[torch.Tensor]
             scale = torch.empty((n_items,), dtype=torch.float32, device=dev) if scale_out is None else scale_out
     pooled = torch.empty((n_items, H), dtype=table.dtype, device=dev) if want_pooled else None
     ln = torch.empty((n_items, H), dtype=table.dtype, device=dev) if (want_ln or mode == L.RB_ACT_NONE) else None
-    gamma = gamma.contiguous()
-    beta = beta.contiguous()
+    gamma = _affine_f32(gamma)
+    beta = _affine_f32(beta)
     if static_scale is not None:
         static_scale = static_scale.contiguous()
     with torch.cuda.device(dev):
@@ -136,8 +169,8 @@ def layernorm_quant(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, ep
     q = torch.empty((n, H), dtype=torch.int8, device=dev) if mode != L.RB_ACT_NONE else None
     scale = torch.empty((n,), dtype=torch.float32, device=dev) if mode == L.RB_ACT_DYNAMIC else None
     ln = torch.empty((n, H), dtype=x.dtype, device=dev) if (want_ln or mode == L.RB_ACT_NONE) else None
-    gamma = gamma.contiguous()
-    beta = beta.contiguous()
+    gamma = _affine_f32(gamma)
+    beta = _affine_f32(beta)
     if static_scale is not None:
         static_scale = static_scale.contiguous()
     with torch.cuda.device(dev):

@@ -61,13 +61,10 @@ def _quantized_weight(rep: nn.Module):
         from .w8a8_triton_kernels import _packed_nk
         return _packed_nk(lin.qweight_t), lin.weight_scale, lin.bias, lin.static_act_scale
     w = lin.weight
-    key = (w.data_ptr(), w._version, w.dtype, w.device)
-    cache = getattr(rep, "_b200_wcache", None)
-    if cache is None or cache[0] != key:
-        q_nk, w_scale = device_ops.quantize_weight_per_channel(w.detach())
-        cache = (key, q_nk, w_scale)
-        rep._b200_wcache = cache
-    return cache[1], cache[2], lin.bias, None
+    q_nk, w_scale = device_ops.cached_derived(w, "w8a8_per_channel",
+                                              lambda x: device_ops.quantize_weight_per_channel(x.detach()))
+    rep._b200_wcache = (None, q_nk, w_scale)
+    return q_nk, w_scale, lin.bias, None
 
 
 def rep_encoder_forward(rep: nn.Module, batch, act_mode: Optional[str] = None,

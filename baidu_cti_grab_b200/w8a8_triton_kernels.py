@@ -20,15 +20,10 @@ and cached for as long as that tensor object lives unmodified.
 
 from __future__ import annotations
 
-import weakref
-
 import torch
 
 from . import _lib, device_ops
 from .w8a8_preprocess import QuantizedWeight
-
-_PACK_CACHE: dict = {}
-
 
 def flatten_input(x: torch.Tensor):
     """Flatten [..., K] -> [M, K] and keep the original leading shape."""
@@ -49,21 +44,7 @@ def _packed_nk(qweight_t: torch.Tensor) -> torch.Tensor:
     if qweight_t.stride(0) == 1 and qweight_t.stride(1) % 16 == 0 and qweight_t.stride(1) >= K \
             and qweight_t.data_ptr() % 16 == 0:
         return qweight_t.t()
-    key = id(qweight_t)
-    hit = _PACK_CACHE.get(key)
-    sig = (qweight_t.data_ptr(), tuple(qweight_t.shape), tuple(qweight_t.stride()), qweight_t._version,
-           qweight_t.device)
-    if hit is not None:
-        ref, hsig, packed = hit
-        if ref() is qweight_t and hsig == sig:
-            return packed
-    packed = device_ops.pack_weight_nk(qweight_t)
-    try:
-        ref = weakref.ref(qweight_t, lambda _r, k=key: _PACK_CACHE.pop(k, None))
-    except TypeError:
-        return packed
-    _PACK_CACHE[key] = (ref, sig, packed)
-    return packed
+    return device_ops.cached_derived(qweight_t, "packed_nk", device_ops.pack_weight_nk)
 
 
 def static_quantize_activation_out(x_2d: torch.Tensor, scale: torch.Tensor, xq: torch.Tensor) -> torch.Tensor:

@@ -54,6 +54,8 @@ def parse_args(argv=None):
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--users", type=int, default=None, help="override users per GPU (default: config's 1024)")
     ap.add_argument("--batches", type=int, default=2, help="distinct synthetic batches cycled per rank")
+    ap.add_argument("--rows-per-slot", type=int, default=None,
+                    help="override table rows per slot (smaller cases for profiling captures)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-items", type=int, default=4096)
@@ -275,6 +277,10 @@ def b200_arm(args):
     _lib.load()
 
     cfg = synth.PROD_BF16_1M
+    if args.rows_per_slot is not None:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, rows_per_slot=args.rows_per_slot,
+                                  name=f"bf16-{args.rows_per_slot}-rows-per-slot")
     users = cfg.num_users if args.users is None else args.users
     bf = torch.bfloat16
 
@@ -438,7 +444,8 @@ def b200_arm(args):
             "data": "synthetic",
             "config": {"workload": cfg.name, "users_per_gpu": users, "items_per_gpu_per_step": int(n_mean),
                        "ids_per_gpu_per_step": int(nnz_mean), "slots": 28, "emb_dim": 512,
-                       "rows_per_slot": cfg.rows_per_slot, "table": "bf16 28.7 GB, one per GPU",
+                       "rows_per_slot": cfg.rows_per_slot,
+                       "table": f"bf16 {cfg.num_rows * 1024 / 1e9:.1f} GB, one per GPU",
                        "linear": "14336->512 W8A8, per-channel weight scales, bf16 out",
                        "act_quant": "dynamic per-token int8", "zipf_a": cfg.zipf_a,
                        "l2": "inputs larger than L2 (28.7 GB table, 1.47 GB int8 activations); no flush",

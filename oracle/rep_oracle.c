@@ -31,11 +31,14 @@
  *
  * Canonical LayerNorm reduction order (shared with the CUDA kernel): a row of
  * S slots x 512 columns is reduced slot by slot.  Inside a slot, "lane" l
- * (0..31) sums its 16 elements, columns 8l..8l+7 then 256+8l..256+8l+7, in
- * that order starting from 0.0f; the 32 lane partials are combined by an
- * xor-butterfly with distances 16, 8, 4, 2, 1 (p[l] = p[l] + p[l^d]); the
- * slot totals are then added in slot order starting from 0.0f.  The first pass
- * sums x, the second pass sums (x - mean)^2 with fmaf(d, d, acc).
+ * (0..31) owns 16 elements, columns 8l..8l+7 then 256+8l..256+8l+7; walking
+ * them in that order, elements at even positions accumulate into a0 and odd
+ * positions into a1 (both from 0.0f), and the lane partial is a0 + a1; the
+ * 32 lane partials are combined by an xor-butterfly with distances 16, 8, 4,
+ * 2, 1 (p[l] = p[l] + p[l^d]); the slot totals are then added in slot order
+ * starting from 0.0f.  The first pass sums x, the second pass sums
+ * (x - mean)^2 with fmaf(d, d, acc).  (The even/odd split is what a packed
+ * two-wide fp32 add computes.)
  *   mean = total1 / H;  var = total2 / H;  rstd = 1.0f / sqrtf(var + eps)
  *   y    = fmaf(rstd * (x - mean), gamma, beta)   (then RNE to the row dtype)
  * Division and square root are IEEE correctly rounded here and in the kernel.
@@ -174,19 +177,19 @@ void rbo_embedding_bag_sum(const void* table, int table_dtype, int64_t num_rows,
 static float canonical_slot_sum(const float* seg, float mean, int centred) {
     float p[32];
     for (int l = 0; l < 32; ++l) {
-        float a = 0.0f;
-        for (int half = 0; half < 2; ++half) {
-            for (int j = 0; j < 8; ++j) {
-                float v = seg[half * 256 + 8 * l + j];
-                if (centred) {
-                    float d = v - mean;
-                    a = fmaf(d, d, a);
-                } else {
-                    a = a + v;
-                }
+        /* lane l's 16 columns in order; even positions feed a0, odd positions a1 */
+        float a[2] = {0.0f, 0.0f};
+        for (int e = 0; e < 16; ++e) {
+            const int col = (e < 8) ? 8 * l + e : 256 + 8 * l + (e - 8);
+            float v = seg[col];
+            if (centred) {
+                float d = v - mean;
+                a[e & 1] = fmaf(d, d, a[e & 1]);
+            } else {
+                a[e & 1] = a[e & 1] + v;
             }
         }
-        p[l] = a;
+        p[l] = a[0] + a[1];
     }
     for (int dist = 16; dist >= 1; dist >>= 1) {
         float q[32];

@@ -142,11 +142,14 @@ def test_weight_quant_matches_torch_formula(cuda_device):
     assert np.array_equal(qw.scale.cpu().numpy(), g["ktail_wscale"])
     w2 = torch.randn(512, 14336, device=cuda_device, dtype=torch.bfloat16)
     qw2 = quantize_weight_per_channel(w2)
-    amax = w2.float().abs().amax(dim=1).clamp(min=1e-8)
+    # the reference's formula evaluated by ATen on the CPU, where x / 127.0 is an
+    # IEEE division (ATen on CUDA multiplies by a rounded reciprocal instead)
+    wc = w2.float().cpu()
+    amax = wc.abs().amax(dim=1).clamp(min=1e-8)
     scale = amax / 127.0
-    ref = torch.round(w2.float() / scale[:, None]).clamp(-128, 127).to(torch.int8)
-    assert torch.equal(qw2.qweight_t.t(), ref)
-    assert torch.equal(qw2.scale, scale)
+    ref = torch.round(wc / scale[:, None]).clamp(-128, 127).to(torch.int8)
+    assert torch.equal(qw2.qweight_t.t().cpu(), ref)
+    assert torch.equal(qw2.scale.cpu(), scale)
     assert qw2.qweight_t.stride() == (1, 14336)
 
 

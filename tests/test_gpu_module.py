@@ -1,0 +1,173 @@
+"""The drop-in RepEncoder (fuse_mode "b200") end to end on the GPU.
+
+* bit-exact against the oracle (K1 + K2 restated on the CPU);
+* against the reference's algorithm run by ATen on the same GPU
+  (nn.EmbeddingBag + cat + nn.LayerNorm in bf16, then the W8A8 quantiser and
+  GEMM): pooled rows bit-exact; bf16 output within the stated tolerance
+  (max-abs <= 2e-2, rel-L2 <= 1e-3);
+* against the fp32 unquantised LayerNorm + Linear (cat_free_layernorm_linear):
+  rel-L2 <= 3e-2.
+"""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS_W8A8 = 2e-2
+REL_L2_W8A8 = 1e-3
+REL_L2_FP32 = 3e-2
+
+
+def _setup(torch, dev, users=96, rows=2000, seed=21):
+    from baidu_cti_grab_b200 import synth
+    from baidu_cti_grab_b200.rep_encoder import RepEncoder
+
+    cfg = synth.WorkloadConfig("module-test", rows, "bfloat16", users, 1, 120, "1+poisson1", 1.1)
+    batch_np = synth.make_batch(cfg, seed=seed)
+    table = synth.make_table_torch(cfg.num_rows, seed=seed, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    H = 28 * 512
+    gamma = (1 + 0.1 * torch.randn(H, device=dev, generator=gen)).to(torch.bfloat16)
+    beta = (0.05 * torch.randn(H, device=dev, generator=gen)).to(torch.bfloat16)
+    # nn.Linear's default initialisation, U(-1/sqrt(H), 1/sqrt(H)) (random-init model weights)
+    w = ((torch.rand(512, H, device=dev, generator=gen) * 2 - 1) / H ** 0.5).to(torch.bfloat16)
+    bias = (0.02 * torch.randn(512, device=dev, generator=gen)).to(torch.bfloat16)
+    rep = RepEncoder.from_parts(table, gamma, beta, w, bias)
+    batch = {"user_offsets": torch.from_numpy(batch_np["user_offsets"]).to(dev)}
+    for s in range(1, 29):
+        batch[s] = [torch.from_numpy(batch_np[s][0]).to(dev), torch.from_numpy(batch_np[s][1])]  # offsets on CPU
+    return rep, batch, batch_np
+
+
+def _rel_l2(a, b):
+    a = a.float()
+    b = b.float()
+    return float((a - b).norm() / b.norm())
+
+
+def test_module_matches_oracle(cuda_device):
+    import torch
+    from oracle import oracle as O
+
+    rep, batch, batch_np = _setup(torch, cuda_device)
+    out, inter = __import__("baidu_cti_grab_b200.rep_encoder", fromlist=["x"]).rep_encoder_forward(
+        rep, batch, return_intermediates=True)
+    torch.cuda.synchronize()
+    table = rep.emb.weight.view(torch.int16).cpu().numpy().view(np.uint16)
+    g = rep.input_norm.weight.float().cpu().numpy()
+    b = rep.input_norm.bias.float().cpu().numpy()
+    oq, oscale = O.rep_forward(table, "bfloat16", batch_np, g, b, 1e-5)
+    assert np.array_equal(inter["q"].cpu().numpy(), oq)
+    assert np.array_equal(inter["scale"].cpu().numpy(), oscale)
+    w_nk, w_scale = rep._b200_wcache[1].cpu().numpy(), rep._b200_wcache[2].cpu().numpy()
+    ref = O.scaled_epilogue(O.gemm_i8_i32(oq, w_nk), oscale, w_scale, rep.linear.bias.float().cpu().numpy(),
+                            "bfloat16")
+    assert np.array_equal(out.float().cpu().numpy(), ref)
+    assert out.dtype == torch.bfloat16 and out.shape == (oq.shape[0], 512)
+
+
+def test_module_against_aten_reference_on_gpu(cuda_device):
+    import torch
+    import torch.nn.functional as F
+    from baidu_cti_grab_b200.rep_encoder import rep_encoder_forward
+
+    rep, batch, _ = _setup(torch, cuda_device, seed=22)
+    out, inter = rep_encoder_forward(rep, batch, return_intermediates=True)
+    # the reference's torch path (models.py:27-47) with ATen's CUDA kernels
+    V = rep.emb.weight.shape[0]
+    pooled = []
+    for s in range(1, 29):
+        v, o = batch[s]
+        o = o.to(v.device)
+        pooled.append(F.embedding_bag(v.clamp(0, V - 1), rep.emb.weight, o[:-1], mode="sum", padding_idx=0))
+    x = torch.cat(pooled, dim=1)
+    assert torch.equal(x, inter["pooled"])
+    ln = F.layer_norm(x, (x.shape[1],), rep.input_norm.weight, rep.input_norm.bias, 1e-5)
+    lnf = ln.double()
+    # LayerNorm rows: ATen reduces in another order -> rare one-ulp differences
+    assert (ln != inter["ln"]).float().mean().item() < 1e-3
+    amax = lnf.abs().amax(dim=1).clamp(min=1e-8)
+    t = lnf * (127.0 / amax)[:, None]  # float64 here: a tolerance check, not a bit-exact one
+    q_ref = (torch.sign(t) * torch.floor(t.abs() + 0.5)).clamp(-128, 127).to(torch.int8)
+    dq = (q_ref.int() - inter["q"].int()).abs()
+    assert dq.max().item() <= 1 and (dq != 0).float().mean().item() < 1e-3
+    w_nk, w_scale = rep._b200_wcache[1], rep._b200_wcache[2]
+    acc = torch._int_mm(q_ref, w_nk.t())
+    sa = (amax / 127.0).float()
+    ref = ((acc.float() * sa[:, None]) * w_scale[None, :] + rep.linear.bias.float()).to(torch.bfloat16)
+    assert (out.float() - ref.float()).abs().max().item() <= MAX_ABS_W8A8
+    assert _rel_l2(out, ref) <= REL_L2_W8A8
+
+
+def test_module_against_fp32_unquantised(cuda_device):
+    import torch
+    from baidu_cti_grab_b200.rep_encoder import rep_encoder_forward
+    from baidu_cti_grab_b200.rep_encoder_fusion import cat_free_layernorm_linear
+
+    rep, batch, _ = _setup(torch, cuda_device, seed=23)
+    out, inter = rep_encoder_forward(rep, batch, return_intermediates=True)
+    pooled = [p.float() for p in inter["pooled"].split(512, dim=1)]
+    ln32 = torch.nn.LayerNorm(28 * 512).to(cuda_device)
+    with torch.no_grad():
+        ln32.weight.copy_(rep.input_norm.weight.float())
+        ln32.bias.copy_(rep.input_norm.bias.float())
+    lin32 = torch.nn.Linear(28 * 512, 512).to(cuda_device)
+    with torch.no_grad():
+        lin32.weight.copy_(rep.linear.weight.float())
+        lin32.bias.copy_(rep.linear.bias.float())
+    with torch.no_grad():
+        ref = cat_free_layernorm_linear(pooled, ln32, lin32)
+    assert _rel_l2(out, ref) <= REL_L2_FP32
+
+
+def test_install_into_reference_shaped_module(cuda_device):
+    """install() adds fuse_mode 'b200' to a RepEncoder class with the reference's layout."""
+    import types
+
+    import torch
+    import torch.nn as nn
+    from baidu_cti_grab_b200.rep_encoder import install, rep_encoder_forward
+
+    class RefLike(nn.Module):  # the reference's attribute layout (models.py:14-22)
+        def __init__(self, rep):
+            super().__init__()
+            self.emb, self.input_norm, self.linear = rep.emb, rep.input_norm, rep.linear
+            self.slot_num, self.fuse_mode = 28, "b200"
+
+        def forward(self, batch):
+            raise AssertionError("reference path must not run for fuse_mode b200")
+
+    rep, batch, _ = _setup(torch, cuda_device, users=8, seed=24)
+    mod = types.SimpleNamespace(RepEncoder=RefLike)
+    install(mod)
+    m = RefLike(rep)
+    out = m(batch)
+    assert torch.equal(out, rep_encoder_forward(rep, batch))
+
+
+def test_static_quantised_checkpoint_layer(cuda_device):
+    """A StaticQuantizedLinear-shaped layer (row-major qweight_t [K,N] buffer, static scale)."""
+    import torch
+    import torch.nn as nn
+    from baidu_cti_grab_b200.rep_encoder import rep_encoder_forward
+    from baidu_cti_grab_b200.w8a8_preprocess import quantize_weight_per_channel
+
+    rep, batch, _ = _setup(torch, cuda_device, users=16, seed=25)
+    qw = quantize_weight_per_channel(rep.linear.weight.float())
+    lin = nn.Module()
+    lin.use_quant = True
+    lin.qweight_t = qw.qweight_t.contiguous()  # row-major [K, N] as in the quantised checkpoint
+    lin.weight_scale = qw.scale.to(torch.bfloat16)  # model.to(bf16) casts the buffers
+    lin.static_act_scale = torch.tensor([0.05], device=cuda_device).to(torch.bfloat16)
+    lin.bias = rep.linear.bias
+    rep.linear = lin
+    out, inter = rep_encoder_forward(rep, batch, return_intermediates=True)
+    assert inter["scale"] is None
+    s = lin.static_act_scale.float()
+    t = (inter["ln"].float() * (1.0 / s)).double()  # fp32 product, rounded half away in float64
+    q_ref = (torch.sign(t) * torch.floor(t.abs() + 0.5)).clamp(-128, 127).to(torch.int8)
+    assert torch.equal(q_ref, inter["q"])
+    acc = torch._int_mm(inter["q"], qw.qweight_t)
+    ref = ((acc.float() * s) * lin.weight_scale.float()[None, :] + lin.bias.float()).to(torch.bfloat16)
+    assert torch.equal(out, ref)
