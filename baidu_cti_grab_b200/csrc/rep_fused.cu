@@ -22,7 +22,6 @@ namespace rb {
 
 constexpr int kSlotsPerWarp = 4;
 constexpr int kDim = 512;
-constexpr int kRowsInFlight = 2;  // table rows a warp holds in registers (the rest are prefetched to L2)
 
 enum RepMode : int { kGatherLnQuant = 0, kGatherPool = 1, kDenseLnQuant = 2 };
 
@@ -131,113 +130,94 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// ------------------------------------------------ row layout per element type
-// A lane's 16 values of a 512-wide slot segment: columns 8l..8l+7 then
-// 256+8l..256+8l+7, held as 8 fp32 pairs (pair p = elements 2p, 2p+1).
-template <typename T>
-struct Seg;
-
-template <>
-struct Seg<__nv_bfloat16> {
-  static constexpr int kBytes = 2;
-  // load 16 values of a bf16 row segment (global or shared) as 8 words
-  __device__ __forceinline__ static void load_words(const __nv_bfloat16* base, int lane, uint32_t* w) {
-    const uint4* p = reinterpret_cast<const uint4*>(base);
-    const uint4 a = p[lane], b = p[32 + lane];
-    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
-    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
-  }
-  __device__ __forceinline__ static void load_pairs(const __nv_bfloat16* base, int lane, F2* x) {
-    uint32_t w[8];
-    load_words(base, lane, w);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = bf2(w[i]);
-  }
-  // round 8 fp32 pairs to bf16 (RNE) and store; returns the rounded pairs in x
-  __device__ __forceinline__ static void round_store(__nv_bfloat16* base, int lane, F2* x) {
-    uint32_t w[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float2 v = un(x[i]);
-      w[i] = pack_bf16x2(v.x, v.y);
-      x[i] = bf2(w[i]);
-    }
-    uint4* p = reinterpret_cast<uint4*>(base);
-    p[lane] = make_uint4(w[0], w[1], w[2], w[3]);
-    p[32 + lane] = make_uint4(w[4], w[5], w[6], w[7]);
-  }
-};
-
-template <>
-struct Seg<float> {
-  static constexpr int kBytes = 4;
-  __device__ __forceinline__ static void load_pairs(const float* base, int lane, F2* x) {
-    const float4* p = reinterpret_cast<const float4*>(base);
-    const float4 a = p[2 * lane], b = p[2 * lane + 1], c = p[64 + 2 * lane], d = p[64 + 2 * lane + 1];
-    x[0] = f2(a.x, a.y); x[1] = f2(a.z, a.w); x[2] = f2(b.x, b.y); x[3] = f2(b.z, b.w);
-    x[4] = f2(c.x, c.y); x[5] = f2(c.z, c.w); x[6] = f2(d.x, d.y); x[7] = f2(d.z, d.w);
-  }
-  __device__ __forceinline__ static void round_store(float* base, int lane, F2* x) {
-    float4* p = reinterpret_cast<float4*>(base);
-    const float2 v0 = un(x[0]), v1 = un(x[1]), v2 = un(x[2]), v3 = un(x[3]);
-    const float2 v4 = un(x[4]), v5 = un(x[5]), v6 = un(x[6]), v7 = un(x[7]);
-    p[2 * lane] = make_float4(v0.x, v0.y, v1.x, v1.y);
-    p[2 * lane + 1] = make_float4(v2.x, v2.y, v3.x, v3.y);
-    p[64 + 2 * lane] = make_float4(v4.x, v4.y, v5.x, v5.y);
-    p[64 + 2 * lane + 1] = make_float4(v6.x, v6.y, v7.x, v7.y);
-  }
-};
-
-// One table row piece of a lane, loaded ahead of its accumulation.
-template <typename T>
-struct RowBuf;
-
-template <>
-struct RowBuf<__nv_bfloat16> {
-  uint4 a, b;
-  __device__ __forceinline__ void load(const __nv_bfloat16* row, int lane) {
-    const uint4* p = reinterpret_cast<const uint4*>(row);
-    a = __ldg(p + lane);
-    b = __ldg(p + 32 + lane);
-  }
-  __device__ __forceinline__ void add_to(F2* acc) const {
-    acc[0] = add2(acc[0], bf2(a.x)); acc[1] = add2(acc[1], bf2(a.y));
-    acc[2] = add2(acc[2], bf2(a.z)); acc[3] = add2(acc[3], bf2(a.w));
-    acc[4] = add2(acc[4], bf2(b.x)); acc[5] = add2(acc[5], bf2(b.y));
-    acc[6] = add2(acc[6], bf2(b.z)); acc[7] = add2(acc[7], bf2(b.w));
-  }
-};
-
-template <>
-struct RowBuf<float> {
-  float4 a, b, c, d;
-  __device__ __forceinline__ void load(const float* row, int lane) {
-    const float4* p = reinterpret_cast<const float4*>(row);
-    a = __ldg(p + 2 * lane);
-    b = __ldg(p + 2 * lane + 1);
-    c = __ldg(p + 64 + 2 * lane);
-    d = __ldg(p + 64 + 2 * lane + 1);
-  }
-  __device__ __forceinline__ void add_to(F2* acc) const {
-    acc[0] = add2(acc[0], f2(a.x, a.y)); acc[1] = add2(acc[1], f2(a.z, a.w));
-    acc[2] = add2(acc[2], f2(b.x, b.y)); acc[3] = add2(acc[3], f2(b.z, b.w));
-    acc[4] = add2(acc[4], f2(c.x, c.y)); acc[5] = add2(acc[5], f2(c.z, c.w));
-    acc[6] = add2(acc[6], f2(d.x, d.y)); acc[7] = add2(acc[7], f2(d.z, d.w));
-  }
-};
-
-// 16 LayerNorm affine parameters of a lane's columns as fp32 pairs (fp32 input)
-__device__ __forceinline__ void load_affine_f32(const float* p, int64_t col0, F2* out) {
-  const float4* q = reinterpret_cast<const float4*>(p + col0);
-  const float4 a = __ldg(q), b = __ldg(q + 1), c = __ldg(q + 64), d = __ldg(q + 65);
-  out[0] = f2(a.x, a.y); out[1] = f2(a.z, a.w); out[2] = f2(b.x, b.y); out[3] = f2(b.z, b.w);
-  out[4] = f2(c.x, c.y); out[5] = f2(c.z, c.w); out[6] = f2(d.x, d.y); out[7] = f2(d.z, d.w);
+// ------------------------------------------ bf16 operands in fp32 arithmetic
+// add/sub.rn.f32.bf16 widen a bf16 operand exactly and round the fp32 result
+// once, i.e. they equal the fp32 op on the unpacked value without the unpack.
+__device__ __forceinline__ float add_lo(float acc, uint32_t w) {
+  float d;
+  asm("{.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tadd.rn.f32.bf16 %0, lo, %2;\n\t}" : "=f"(d) : "r"(w), "f"(acc));
+  return d;
+}
+__device__ __forceinline__ float add_hi(float acc, uint32_t w) {
+  float d;
+  asm("{.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tadd.rn.f32.bf16 %0, hi, %2;\n\t}" : "=f"(d) : "r"(w), "f"(acc));
+  return d;
+}
+__device__ __forceinline__ float sub_lo(uint32_t w, float m) {  // bf16(lo) - m
+  float d;
+  asm("{.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tsub.rn.f32.bf16 %0, lo, %2;\n\t}" : "=f"(d) : "r"(w), "f"(m));
+  return d;
+}
+__device__ __forceinline__ float sub_hi(uint32_t w, float m) {  // bf16(hi) - m
+  float d;
+  asm("{.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tsub.rn.f32.bf16 %0, hi, %2;\n\t}" : "=f"(d) : "r"(w), "f"(m));
+  return d;
 }
 
-// same for 16-bit (bf16 / fp16) parameters
+// ------------------------------------------------ row pieces per element type
+// A lane's 16 values of a 512-wide slot segment are columns 8l..8l+7 and
+// 256+8l..256+8l+7.  bf16 rows travel as 8 packed words (w[i] = elements
+// 2i, 2i+1); fp32 rows as 8 fp32 pairs.
+__device__ __forceinline__ void ldg_words(const void* seg, int lane, uint32_t* w) {
+  const uint4* p = reinterpret_cast<const uint4*>(seg);
+  const uint4 a = __ldg(p + lane), b = __ldg(p + 32 + lane);
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+__device__ __forceinline__ void st_words(void* seg, int lane, const uint32_t* w) {
+  uint4* p = reinterpret_cast<uint4*>(seg);
+  p[lane] = make_uint4(w[0], w[1], w[2], w[3]);
+  p[32 + lane] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+__device__ __forceinline__ void ld_words(const void* seg, int lane, uint32_t* w) {  // shared or global, cached
+  const uint4* p = reinterpret_cast<const uint4*>(seg);
+  const uint4 a = p[lane], b = p[32 + lane];
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+__device__ __forceinline__ void ldg_pairs(const float* seg, int lane, F2* x) {
+  const float4* p = reinterpret_cast<const float4*>(seg);
+  const float4 a = __ldg(p + 2 * lane), b = __ldg(p + 2 * lane + 1), c = __ldg(p + 64 + 2 * lane),
+               d = __ldg(p + 64 + 2 * lane + 1);
+  x[0] = f2(a.x, a.y); x[1] = f2(a.z, a.w); x[2] = f2(b.x, b.y); x[3] = f2(b.z, b.w);
+  x[4] = f2(c.x, c.y); x[5] = f2(c.z, c.w); x[6] = f2(d.x, d.y); x[7] = f2(d.z, d.w);
+}
+__device__ __forceinline__ void stg_pairs(float* seg, int lane, const F2* x) {
+  float4* p = reinterpret_cast<float4*>(seg);
+  const float2 v0 = un(x[0]), v1 = un(x[1]), v2 = un(x[2]), v3 = un(x[3]);
+  const float2 v4 = un(x[4]), v5 = un(x[5]), v6 = un(x[6]), v7 = un(x[7]);
+  p[2 * lane] = make_float4(v0.x, v0.y, v1.x, v1.y);
+  p[2 * lane + 1] = make_float4(v2.x, v2.y, v3.x, v3.y);
+  p[64 + 2 * lane] = make_float4(v4.x, v4.y, v5.x, v5.y);
+  p[64 + 2 * lane + 1] = make_float4(v6.x, v6.y, v7.x, v7.y);
+}
+// fp32 row in shared memory, lane-major per slot (conflict-free 16-byte accesses):
+// chunk c (0..3) of lane l of slot s = pairs 2c, 2c+1, at float s*512 + c*128 + 4l
+__device__ __forceinline__ void sts_pairs(float* row, int s, int lane, const F2* x) {
+  float4* p = reinterpret_cast<float4*>(row + s * kDim) + lane;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float2 u = un(x[2 * c]), v = un(x[2 * c + 1]);
+    p[32 * c] = make_float4(u.x, u.y, v.x, v.y);
+  }
+}
+__device__ __forceinline__ void lds_pairs(const float* row, int s, int lane, F2* x) {
+  const float4* p = reinterpret_cast<const float4*>(row + s * kDim) + lane;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float4 v = p[32 * c];
+    x[2 * c] = f2(v.x, v.y);
+    x[2 * c + 1] = f2(v.z, v.w);
+  }
+}
+
+// 16 LayerNorm affine parameters of a lane's columns as fp32 pairs
 __device__ __forceinline__ void load_affine(const void* p, int dtype, int64_t col0, F2* out) {
   if (dtype == RB_F32) {
-    load_affine_f32(reinterpret_cast<const float*>(p), col0, out);
+    const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + col0);
+    const float4 a = __ldg(q), b = __ldg(q + 1), c = __ldg(q + 64), d = __ldg(q + 65);
+    out[0] = f2(a.x, a.y); out[1] = f2(a.z, a.w); out[2] = f2(b.x, b.y); out[3] = f2(b.z, b.w);
+    out[4] = f2(c.x, c.y); out[5] = f2(c.z, c.w); out[6] = f2(d.x, d.y); out[7] = f2(d.z, d.w);
     return;
   }
   const uint4* q = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + col0);
@@ -252,26 +232,6 @@ __device__ __forceinline__ void load_affine(const void* p, int dtype, int64_t co
       out[i] = f2(h.x, h.y);
     }
   }
-}
-
-// canonical lane partial of 8 pairs: even positions in .x, odd in .y, then x + y
-__device__ __forceinline__ float lane_partial(const F2* x) {
-  F2 a = f2(0.0f, 0.0f);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) a = add2(a, x[i]);
-  const float2 v = un(a);
-  return __fadd_rn(v.x, v.y);
-}
-
-__device__ __forceinline__ float lane_partial_sq(const F2* x, F2 mean2) {
-  F2 a = f2(0.0f, 0.0f);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const F2 d = sub2(x[i], mean2);
-    a = fma2(d, d, a);
-  }
-  const float2 v = un(a);
-  return __fadd_rn(v.x, v.y);
 }
 
 // Ask the copy engine to bring `bytes` at `p` into L2 (no registers, no wait).
@@ -291,19 +251,25 @@ __device__ __forceinline__ V sel4(const V* a, int j) {
   return j == 0 ? a[0] : (j == 1 ? a[1] : (j == 2 ? a[2] : a[3]));
 }
 
-// One CTA per item.  Warp w owns slots 4w..4w+3: it gathers their bags with
-// kRowsInFlight rows in flight, rounds each bag sum to the row dtype into the
-// shared-memory row (S*512 values) and contributes the slot's first-pass
-// LayerNorm partial.  The remaining passes read the row back from shared
-// memory: variance, normalise + affine (written back in place) with the
-// absmax, then the int8 quantiser.  gamma/beta arrive as fp32.
+// One CTA per item.  Warp w owns slots 4w..4w+3.  Per slot it sums the bag's
+// table rows in bag order (kRows loads in flight; every row of the warp's id
+// window was already requested into L2 by a bulk prefetch), rounds the sum to
+// the row dtype into the shared-memory row and adds the slot's first-pass
+// LayerNorm partial (canonical order: even / odd accumulators per lane,
+// butterfly, slot order).  Then: variance pass, normalise + affine (y rounded
+// to the row dtype, written back in place) with the absmax, and the int8
+// quantiser.  bf16 rows stay packed in shared memory (28 KB per item) and
+// enter fp32 arithmetic through the mixed-precision add/sub.
 template <typename T, int MODE>
 __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant__ RepParams p) {
-  extern __shared__ __align__(16) uint8_t s_row_raw[];
-  T* s_row = reinterpret_cast<T*>(s_row_raw);
+  constexpr bool kBf16 = sizeof(T) == 2;
+  constexpr int kRows = kBf16 ? 3 : 2;  // table rows a warp holds in registers
+  extern __shared__ __align__(16) uint8_t s_raw[];
   __shared__ float s_tot[RB_MAX_SLOTS];
   __shared__ float s_wmax[8];
   __shared__ float s_stat[4];  // mean, rstd, scale, inv
+  uint32_t* s_words = reinterpret_cast<uint32_t*>(s_raw);  // bf16 row: 256 words per slot
+  float* s_f32 = reinterpret_cast<float*>(s_raw);          // fp32 row: 512 floats per slot
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -312,15 +278,69 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
   const int slot0 = warp * kSlotsPerWarp;
   const int nsl = max(0, min(kSlotsPerWarp, S - slot0));
 
+  // pooled slot j of this warp is final in `acc` (fp32, not yet rounded):
+  // round to T, keep it in shared memory, emit the first-pass partial
+  auto finish_slot = [&](int s, float* acc) {
+    float a0 = 0.0f, a1 = 0.0f;
+    if constexpr (kBf16) {
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
+      st_words(s_words + s * 256, lane, w);
+      if constexpr (MODE == kGatherPool) {
+        st_words(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)p.slots.col_slot[s] * kDim, lane, w);
+      } else if (p.pooled != nullptr) {
+        st_words(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, w);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        a0 = add_lo(a0, w[i]);
+        a1 = add_hi(a1, w[i]);
+      }
+    } else {
+      F2 x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = f2(acc[2 * i], acc[2 * i + 1]);
+      sts_pairs(s_f32, s, lane, x);
+      if constexpr (MODE == kGatherPool) {
+        stg_pairs(reinterpret_cast<float*>(p.pooled) + item * p.ldp + (int64_t)p.slots.col_slot[s] * kDim, lane, x);
+      } else if (p.pooled != nullptr) {
+        stg_pairs(reinterpret_cast<float*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, x);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        a0 = __fadd_rn(a0, acc[2 * i]);
+        a1 = __fadd_rn(a1, acc[2 * i + 1]);
+      }
+    }
+    const float a = warp_sum_butterfly(__fadd_rn(a0, a1));
+    if (lane == 0) s_tot[s] = a;
+  };
+
   if constexpr (MODE == kDenseLnQuant) {
     const T* xrow = reinterpret_cast<const T*>(p.x) + item * p.ldx;
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
-      F2 x[8];
-      Seg<T>::load_pairs(xrow + (int64_t)s * kDim, lane, x);
-      Seg<T>::round_store(s_row + s * kDim, lane, x);  // identity rounding: values are already T
-      const float a = warp_sum_butterfly(lane_partial(x));
-      if (lane == 0) s_tot[s] = a;
+      float acc[16];
+      if constexpr (kBf16) {
+        uint32_t w[8];
+        ldg_words(xrow + (int64_t)s * kDim, lane, w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          acc[2 * i] = bf16_lo(w[i]);
+          acc[2 * i + 1] = bf16_hi(w[i]);
+        }
+      } else {
+        F2 x[8];
+        ldg_pairs(xrow + (int64_t)s * kDim, lane, x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float2 v = un(x[i]);
+          acc[2 * i] = v.x;
+          acc[2 * i + 1] = v.y;
+        }
+      }
+      finish_slot(s, acc);
     }
   } else {
     // ---- bag bounds of this warp's slots: lanes 0-3 starts, lanes 4-7 ends
@@ -349,62 +369,73 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
 
     const T* table = reinterpret_cast<const T*>(p.table);
     const int vmax = (int)(p.num_rows - 1);
-    F2 acc[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = f2(0.0f, 0.0f);
-    int cur = 0;  // slot (0..nsl) whose bag is being summed
-
-    auto finish_slot = [&](int j) {
-      const int s = slot0 + j;
-      Seg<T>::round_store(s_row + s * kDim, lane, acc);  // nn.EmbeddingBag output dtype
-      const float a = warp_sum_butterfly(lane_partial(acc));
-      if (lane == 0) s_tot[s] = a;
-      if constexpr (MODE == kGatherPool) {
-        Seg<T>::round_store(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)p.slots.col_slot[s] * kDim,
-                            lane, acc);
-      } else {
-        if (p.pooled != nullptr)
-          Seg<T>::round_store(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, acc);
+    // ids of flattened positions w0 .. w0+31, one per lane; each row is
+    // requested into L2 as soon as its id is known
+    auto load_window = [&](int w0) {
+      const int t = w0 + lane;
+      int id = 0;
+      if (t < total) {
+        const int j = (t >= pre[1]) + (t >= pre[2]) + (t >= pre[3]);
+        const int64_t v = p.slots.values[slot0 + j][sel4(start, j) + (t - sel4(pre, j))];
+        id = (int)(v < 0 ? 0 : (v > vmax ? vmax : v));
+        if (id != 0) prefetch_l2_bulk(table + (int64_t)id * kDim, kDim * (int)sizeof(T));
       }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = f2(0.0f, 0.0f);
+      return id;
     };
+    int w0 = 0;
+    int my_id = load_window(0);
 
-    for (int w0 = 0; w0 < total; w0 += 32) {
-      // row ids of positions w0 .. w0+31 of the warp's concatenated bag list
-      int my_id = 0;
-      {
-        const int t = w0 + lane;
-        if (t < total) {
-          const int j = (t >= pre[1]) + (t >= pre[2]) + (t >= pre[3]);
-          int64_t id = p.slots.values[slot0 + j][sel4(start, j) + (t - sel4(pre, j))];
-          my_id = (int)(id < 0 ? 0 : (id > vmax ? vmax : id));
-          // every row of the window is requested at once; the register
-          // pipeline below then mostly hits L2
-          if (my_id != 0) prefetch_l2_bulk(table + (int64_t)my_id * kDim, kDim * Seg<T>::kBytes);
-        }
-      }
-      const int nwin = min(32, total - w0);
-      for (int u0 = 0; u0 < nwin; u0 += kRowsInFlight) {
-        RowBuf<T> buf[kRowsInFlight];
-        int ids[kRowsInFlight];
+    for (int j = 0; j < nsl; ++j) {
+      const int tend = pre[j + 1];
+      float acc[16];
 #pragma unroll
-        for (int u = 0; u < kRowsInFlight; ++u) {
-          ids[u] = __shfl_sync(0xffffffffu, my_id, (u0 + u) & 31);
-          if (u0 + u < nwin && ids[u] != 0) buf[u].load(table + (int64_t)ids[u] * kDim, lane);
+      for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
+      for (int t = pre[j]; t < tend; t += kRows) {
+        if (t + kRows > w0 + 32) {  // warp-uniform: slide the id window
+          w0 = t;
+          my_id = load_window(w0);
         }
+        int ids[kRows];
 #pragma unroll
-        for (int u = 0; u < kRowsInFlight; ++u) {
-          if (u0 + u < nwin) {
-            const int t = w0 + u0 + u;
-            const int j = (t >= pre[1]) + (t >= pre[2]) + (t >= pre[3]);
-            while (cur < j) finish_slot(cur++);
-            if (ids[u] != 0) buf[u].add_to(acc);  // padding_idx 0 is excluded
+        for (int u = 0; u < kRows; ++u) {
+          ids[u] = __shfl_sync(0xffffffffu, my_id, (t + u - w0) & 31);
+          if (t + u >= tend) ids[u] = 0;
+        }
+        if constexpr (kBf16) {
+          uint32_t buf[kRows][8];
+#pragma unroll
+          for (int u = 0; u < kRows; ++u)
+            if (ids[u] != 0) ldg_words(table + (int64_t)ids[u] * kDim, lane, buf[u]);
+#pragma unroll
+          for (int u = 0; u < kRows; ++u) {
+            if (ids[u] != 0) {  // padding_idx 0 is excluded; bag order kept
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                acc[2 * i] = add_lo(acc[2 * i], buf[u][i]);
+                acc[2 * i + 1] = add_hi(acc[2 * i + 1], buf[u][i]);
+              }
+            }
+          }
+        } else {
+          F2 buf[kRows][8];
+#pragma unroll
+          for (int u = 0; u < kRows; ++u)
+            if (ids[u] != 0) ldg_pairs(reinterpret_cast<const float*>(table) + (int64_t)ids[u] * kDim, lane, buf[u]);
+#pragma unroll
+          for (int u = 0; u < kRows; ++u) {
+            if (ids[u] != 0) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float2 v = un(buf[u][i]);
+                acc[2 * i] = __fadd_rn(acc[2 * i], v.x);
+                acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], v.y);
+              }
+            }
           }
         }
       }
+      finish_slot(slot0 + j, acc);
     }
-    while (cur < nsl) finish_slot(cur++);
   }
 
   if constexpr (MODE != kGatherPool) {
@@ -421,10 +452,27 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
     // ---- pass 2: variance around the mean
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
-      F2 x[8];
-      Seg<T>::load_pairs(s_row + s * kDim, lane, x);
-      const float a = warp_sum_butterfly(lane_partial_sq(x, mean2));
-      if (lane == 0) s_tot[s] = a;
+      F2 a = f2(0.0f, 0.0f);
+      if constexpr (kBf16) {
+        uint32_t w[8];
+        ld_words(s_words + s * 256, lane, w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const F2 d = f2(sub_lo(w[i], mean), sub_hi(w[i], mean));
+          a = fma2(d, d, a);
+        }
+      } else {
+        F2 x[8];
+        lds_pairs(s_f32, s, lane, x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const F2 d = sub2(x[i], mean2);
+          a = fma2(d, d, a);
+        }
+      }
+      const float2 v = un(a);
+      const float t = warp_sum_butterfly(__fadd_rn(v.x, v.y));
+      if (lane == 0) s_tot[s] = t;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -436,24 +484,44 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
     __syncthreads();
     const float rstd = s_stat[1];
     const F2 rstd2 = f2(rstd, rstd);
-    // ---- pass 3: y = fma(rstd * (x - mean), gamma, beta), rounded to T, in place; absmax
+    // ---- pass 3: y = fma(rstd * (x - mean), gamma, beta) rounded to T, in place; absmax
     float amax = 0.0f;
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
-      F2 x[8], g[8], b[8];
-      Seg<T>::load_pairs(s_row + s * kDim, lane, x);
+      F2 g[8], b[8], y[8];
       const int64_t col0 = (int64_t)s * kDim + 8 * lane;
       load_affine(p.gamma, p.ln_dtype, col0, g);
       load_affine(p.beta, p.ln_dtype, col0, b);
+      if constexpr (kBf16) {
+        uint32_t w[8];
+        ld_words(s_words + s * 256, lane, w);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = fma2(mul2(rstd2, sub2(x[i], mean2)), g[i], b[i]);
-      Seg<T>::round_store(s_row + s * kDim, lane, x);
+        for (int i = 0; i < 8; ++i) {
+          const F2 d = f2(sub_lo(w[i], mean), sub_hi(w[i], mean));
+          const float2 v = un(fma2(mul2(rstd2, d), g[i], b[i]));
+          w[i] = pack_bf16x2(v.x, v.y);
+        }
+        st_words(s_words + s * 256, lane, w);
+        if (p.ln != nullptr) st_words(reinterpret_cast<T*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, w);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float2 v = un(x[i]);
-        amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
+        for (int i = 0; i < 8; ++i) {
+          // |bf16| ordered as unsigned 16-bit integers; widened exactly at the end
+          const uint32_t m = w[i] & 0x7fff7fffu;
+          amax = fmaxf(amax, fmaxf(bf16_lo(m), bf16_hi(m)));
+        }
+      } else {
+        F2 x[8];
+        lds_pairs(s_f32, s, lane, x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = fma2(mul2(rstd2, sub2(x[i], mean2)), g[i], b[i]);
+        sts_pairs(s_f32, s, lane, y);
+        if (p.ln != nullptr) stg_pairs(reinterpret_cast<float*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, y);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float2 v = un(y[i]);
+          amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
+        }
       }
-      if (p.ln != nullptr) Seg<T>::round_store(reinterpret_cast<T*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, x);
     }
     if (p.act_mode == RB_ACT_NONE) return;
     amax = warp_max(amax);
@@ -465,9 +533,8 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
         float m = 0.0f;
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, s_wmax[w]);
         m = fmaxf(m, 1e-8f);
-        const float sc = __fdiv_rn(m, 127.0f);
+        p.scale[item] = __fdiv_rn(m, 127.0f);
         inv = __fdiv_rn(127.0f, m);
-        p.scale[item] = sc;
       } else {
         inv = __fdiv_rn(1.0f, load_as_f32(p.static_scale, p.static_scale_dtype, 0));
       }
@@ -481,7 +548,14 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
       F2 x[8];
-      Seg<T>::load_pairs(s_row + s * kDim, lane, x);
+      if constexpr (kBf16) {
+        uint32_t w[8];
+        ld_words(s_words + s * 256, lane, w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = bf2(w[i]);
+      } else {
+        lds_pairs(s_f32, s, lane, x);
+      }
       int q[16];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -533,6 +607,7 @@ static int launch_rep(const RepParams& p, int row_dtype, cudaStream_t stream) {
   if (p.num_items == 0) return RB_OK;
   const int warps = (p.num_slots + kSlotsPerWarp - 1) / kSlotsPerWarp;
   dim3 grid((unsigned)p.num_items), block(32 * warps);
+  // the item's pooled row: packed bf16, or fp32 for fp32 tables
   const size_t smem = (size_t)p.num_slots * kDim * dtype_size(row_dtype);
   cudaError_t e = cudaSuccess;
   if (row_dtype == RB_BF16) {
