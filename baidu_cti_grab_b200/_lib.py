@@ -33,6 +33,8 @@ SIGNATURES = {
     "rb_rep_gather_pool": [_vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64, _vp],
     "rb_layernorm_quant": [_vp, _i32, _i64, _i32, _i64, _vp, _vp, _i32, _f32, _i32, _vp, _i32, _vp, _i64,
                            _vp, _vp, _vp],
+    "rb_layernorm_quant_slots": [_vp, _i32, _i64, _i32, _i64, _vp, _vp, _i32, _f32, _i32, _vp, _i32, _vp, _i64,
+                                 _vp, _vp, _vp],
     "rb_quant_dynamic_per_token": [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp],
     "rb_quant_static": [_vp, _i32, _i64, _vp, _i32, _vp, _vp],
     "rb_quant_rows_v1": [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp],

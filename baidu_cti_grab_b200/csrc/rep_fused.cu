@@ -21,6 +21,9 @@
 namespace rb {
 
 constexpr int kSlotsPerWarp = 4;
+#ifndef RB_K1_BF16_ROWS
+#define RB_K1_BF16_ROWS 3
+#endif
 constexpr int kDim = 512;
 
 enum RepMode : int { kGatherLnQuant = 0, kGatherPool = 1, kDenseLnQuant = 2 };
@@ -36,7 +39,7 @@ struct RepParams {
   SlotArgs slots;
   const void* table;
   int64_t num_rows;
-  const void* x;  // dense pooled rows (kDenseLnQuant)
+  const void* xs[RB_MAX_SLOTS];  // dense pooled rows (kDenseLnQuant): slot s of item i at xs[s] + i*ldx
   int64_t ldx;
   int num_slots;
   int64_t num_items;
@@ -118,10 +121,24 @@ __device__ __forceinline__ uint32_t pack_i8x4_prmt(int a, int b, int c, int d) {
   return __byte_perm(ab, cd, 0x5410);
 }
 
-__device__ __forceinline__ float warp_sum_butterfly(float v) {
-#pragma unroll
-  for (int d = 16; d >= 1; d >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, d));
-  return v;
+// Canonical butterfly of four slots' lane partials at once.  Each step adds
+// the same pairs as a per-slot xor-butterfly (16, 8, 4, 2, 1), but after the
+// first two steps a lane only carries the slot it will finish: lanes 0-7 end
+// with slot 0's total, 8-15 slot 1, 16-23 slot 2, 24-31 slot 3.
+__device__ __forceinline__ float warp_sum4_butterfly(float v0, float v1, float v2, float v3, int lane) {
+  const bool lo16 = lane < 16;
+  float k0 = lo16 ? v0 : v2, k1 = lo16 ? v1 : v3;
+  const float o0 = lo16 ? v2 : v0, o1 = lo16 ? v3 : v1;
+  k0 = __fadd_rn(k0, __shfl_xor_sync(0xffffffffu, o0, 16));
+  k1 = __fadd_rn(k1, __shfl_xor_sync(0xffffffffu, o1, 16));
+  const bool lo8 = (lane & 8) == 0;
+  float k = lo8 ? k0 : k1;
+  const float o = lo8 ? k1 : k0;
+  k = __fadd_rn(k, __shfl_xor_sync(0xffffffffu, o, 8));
+  k = __fadd_rn(k, __shfl_xor_sync(0xffffffffu, k, 4));
+  k = __fadd_rn(k, __shfl_xor_sync(0xffffffffu, k, 2));
+  k = __fadd_rn(k, __shfl_xor_sync(0xffffffffu, k, 1));
+  return k;
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -263,7 +280,7 @@ __device__ __forceinline__ V sel4(const V* a, int j) {
 template <typename T, int MODE>
 __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant__ RepParams p) {
   constexpr bool kBf16 = sizeof(T) == 2;
-  constexpr int kRows = kBf16 ? 3 : 2;  // table rows a warp holds in registers
+  constexpr int kRows = kBf16 ? RB_K1_BF16_ROWS : 2;  // table rows a warp holds in registers
   extern __shared__ __align__(16) uint8_t s_raw[];
   __shared__ float s_tot[RB_MAX_SLOTS];
   __shared__ float s_wmax[8];
@@ -278,9 +295,9 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
   const int slot0 = warp * kSlotsPerWarp;
   const int nsl = max(0, min(kSlotsPerWarp, S - slot0));
 
-  // pooled slot j of this warp is final in `acc` (fp32, not yet rounded):
-  // round to T, keep it in shared memory, emit the first-pass partial
-  auto finish_slot = [&](int s, float* acc) {
+  // pooled slot s of this warp is final in `acc` (fp32, not yet rounded):
+  // round to T, keep it in shared memory, return the lane's first-pass partial
+  auto finish_slot = [&](int s, float* acc) -> float {
     float a0 = 0.0f, a1 = 0.0f;
     if constexpr (kBf16) {
       uint32_t w[8];
@@ -313,18 +330,29 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
         a1 = __fadd_rn(a1, acc[2 * i + 1]);
       }
     }
-    const float a = warp_sum_butterfly(__fadd_rn(a0, a1));
-    if (lane == 0) s_tot[s] = a;
+    return __fadd_rn(a0, a1);
+  };
+  // lane partials of the warp's slots (0 for slots past S), reduced together
+  float part[kSlotsPerWarp] = {0.0f, 0.0f, 0.0f, 0.0f};
+  auto put_part = [&](int j, float v) {
+#pragma unroll
+    for (int jj = 0; jj < kSlotsPerWarp; ++jj)
+      if (jj == j) part[jj] = v;
+  };
+  auto reduce_parts = [&]() {
+    const float t = warp_sum4_butterfly(part[0], part[1], part[2], part[3], lane);
+    const int j = lane >> 3;
+    if ((lane & 7) == 0 && j < nsl) s_tot[slot0 + j] = t;
   };
 
   if constexpr (MODE == kDenseLnQuant) {
-    const T* xrow = reinterpret_cast<const T*>(p.x) + item * p.ldx;
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
+      const T* xseg = reinterpret_cast<const T*>(p.xs[s]) + item * p.ldx;
       float acc[16];
       if constexpr (kBf16) {
         uint32_t w[8];
-        ldg_words(xrow + (int64_t)s * kDim, lane, w);
+        ldg_words(xseg, lane, w);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           acc[2 * i] = bf16_lo(w[i]);
@@ -332,7 +360,7 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
         }
       } else {
         F2 x[8];
-        ldg_pairs(xrow + (int64_t)s * kDim, lane, x);
+        ldg_pairs(reinterpret_cast<const float*>(xseg), lane, x);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float2 v = un(x[i]);
@@ -340,7 +368,7 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
           acc[2 * i + 1] = v.y;
         }
       }
-      finish_slot(s, acc);
+      put_part(j, finish_slot(s, acc));
     }
   } else {
     // ---- bag bounds of this warp's slots: lanes 0-3 starts, lanes 4-7 ends
@@ -434,11 +462,12 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
           }
         }
       }
-      finish_slot(slot0 + j, acc);
+      put_part(j, finish_slot(slot0 + j, acc));
     }
   }
 
   if constexpr (MODE != kGatherPool) {
+    reduce_parts();
     const float H = (float)(S * kDim);
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -450,6 +479,8 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
     const float mean = s_stat[0];
     const F2 mean2 = f2(mean, mean);
     // ---- pass 2: variance around the mean
+#pragma unroll
+    for (int jj = 0; jj < kSlotsPerWarp; ++jj) part[jj] = 0.0f;
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
       F2 a = f2(0.0f, 0.0f);
@@ -471,9 +502,9 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
         }
       }
       const float2 v = un(a);
-      const float t = warp_sum_butterfly(__fadd_rn(v.x, v.y));
-      if (lane == 0) s_tot[s] = t;
+      put_part(j, __fadd_rn(v.x, v.y));
     }
+    reduce_parts();
     __syncthreads();
     if (threadIdx.x == 0) {
       float t = 0.0f;
@@ -499,16 +530,13 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
         for (int i = 0; i < 8; ++i) {
           const F2 d = f2(sub_lo(w[i], mean), sub_hi(w[i], mean));
           const float2 v = un(fma2(mul2(rstd2, d), g[i], b[i]));
+          // rounding to bf16 is monotonic and symmetric, so the absmax of the
+          // rounded row is the rounded absmax of the fp32 row
+          amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
           w[i] = pack_bf16x2(v.x, v.y);
         }
         st_words(s_words + s * 256, lane, w);
         if (p.ln != nullptr) st_words(reinterpret_cast<T*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, w);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          // |bf16| ordered as unsigned 16-bit integers; widened exactly at the end
-          const uint32_t m = w[i] & 0x7fff7fffu;
-          amax = fmaxf(amax, fmaxf(bf16_lo(m), bf16_hi(m)));
-        }
       } else {
         F2 x[8];
         lds_pairs(s_f32, s, lane, x);
@@ -524,6 +552,7 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
       }
     }
     if (p.act_mode == RB_ACT_NONE) return;
+    if constexpr (kBf16) amax = round_bf16(amax);
     amax = warp_max(amax);
     if (lane == 0) s_wmax[warp] = amax;
     __syncthreads();
@@ -731,23 +760,13 @@ extern "C" int rb_rep_gather_pool(const void* table, int table_dtype, int64_t nu
   return launch_rep<kGatherPool>(p, table_dtype, (cudaStream_t)stream);
 }
 
-extern "C" int rb_layernorm_quant(const void* x, int x_dtype, int64_t num_items, int num_slots, int64_t ldx,
-                                  const void* ln_gamma, const void* ln_beta, int ln_dtype, float eps,
-                                  int act_mode, const void* static_scale, int static_scale_dtype,
-                                  int8_t* q_out, int64_t ldq, float* scale_out, void* ln_out, void* stream) {
-  int rc = validate_common(num_slots, num_items);
+static int layernorm_quant_common(RepParams& p, int x_dtype, int64_t num_items, int num_slots, int64_t ldx,
+                                  const void* ln_gamma, const void* ln_beta, int ln_dtype, float eps, int act_mode,
+                                  const void* static_scale, int static_scale_dtype, int8_t* q_out, int64_t ldq,
+                                  float* scale_out, void* ln_out, void* stream) {
+  int rc = check_ln_args(ln_gamma, ln_beta, ln_dtype, act_mode, static_scale, static_scale_dtype, q_out, ldq,
+                         scale_out, ln_out, num_slots);
   if (rc) return rc;
-  if (x_dtype != RB_BF16 && x_dtype != RB_F32) return fail(RB_ERR_VALUE, "x dtype must be RB_BF16 or RB_F32");
-  if (num_items == 0) return RB_OK;
-  const int esz = dtype_size(x_dtype);
-  if (x == nullptr || !aligned(x, 16) || (ldx * esz) % 16 != 0 || ldx < (int64_t)num_slots * kDim)
-    return fail(RB_ERR_VALUE, "x must be 16-byte aligned with 16-byte row stride and ldx >= %d",
-                num_slots * kDim);
-  rc = check_ln_args(ln_gamma, ln_beta, ln_dtype, act_mode, static_scale, static_scale_dtype, q_out, ldq,
-                     scale_out, ln_out, num_slots);
-  if (rc) return rc;
-  RepParams p{};
-  p.x = x;
   p.ldx = ldx;
   p.num_slots = num_slots;
   p.num_items = num_items;
@@ -763,4 +782,44 @@ extern "C" int rb_layernorm_quant(const void* x, int x_dtype, int64_t num_items,
   p.scale = scale_out;
   p.ln = ln_out;
   return launch_rep<kDenseLnQuant>(p, x_dtype, (cudaStream_t)stream);
+}
+
+extern "C" int rb_layernorm_quant(const void* x, int x_dtype, int64_t num_items, int num_slots, int64_t ldx,
+                                  const void* ln_gamma, const void* ln_beta, int ln_dtype, float eps,
+                                  int act_mode, const void* static_scale, int static_scale_dtype,
+                                  int8_t* q_out, int64_t ldq, float* scale_out, void* ln_out, void* stream) {
+  int rc = validate_common(num_slots, num_items);
+  if (rc) return rc;
+  if (x_dtype != RB_BF16 && x_dtype != RB_F32) return fail(RB_ERR_VALUE, "x dtype must be RB_BF16 or RB_F32");
+  if (num_items == 0) return RB_OK;
+  const int esz = dtype_size(x_dtype);
+  if (x == nullptr || !aligned(x, 16) || (ldx * esz) % 16 != 0 || ldx < (int64_t)num_slots * kDim)
+    return fail(RB_ERR_VALUE, "x must be 16-byte aligned with 16-byte row stride and ldx >= %d",
+                num_slots * kDim);
+  RepParams p{};
+  for (int s = 0; s < num_slots; ++s) p.xs[s] = reinterpret_cast<const char*>(x) + (int64_t)s * kDim * esz;
+  return layernorm_quant_common(p, x_dtype, num_items, num_slots, ldx, ln_gamma, ln_beta, ln_dtype, eps, act_mode,
+                                static_scale, static_scale_dtype, q_out, ldq, scale_out, ln_out, stream);
+}
+
+extern "C" int rb_layernorm_quant_slots(const void* const* slot_rows, int x_dtype, int64_t num_items,
+                                        int num_slots, int64_t ld, const void* ln_gamma, const void* ln_beta,
+                                        int ln_dtype, float eps, int act_mode, const void* static_scale,
+                                        int static_scale_dtype, int8_t* q_out, int64_t ldq, float* scale_out,
+                                        void* ln_out, void* stream) {
+  int rc = validate_common(num_slots, num_items);
+  if (rc) return rc;
+  if (x_dtype != RB_BF16 && x_dtype != RB_F32) return fail(RB_ERR_VALUE, "x dtype must be RB_BF16 or RB_F32");
+  if (num_items == 0) return RB_OK;
+  const int esz = dtype_size(x_dtype);
+  if (slot_rows == nullptr || (ld * esz) % 16 != 0 || ld < kDim)
+    return fail(RB_ERR_VALUE, "slot rows need a 16-byte row stride ld >= 512");
+  RepParams p{};
+  for (int s = 0; s < num_slots; ++s) {
+    if (slot_rows[s] == nullptr || !aligned(slot_rows[s], 16))
+      return fail(RB_ERR_VALUE, "slot %d rows must be 16-byte aligned", s);
+    p.xs[s] = slot_rows[s];
+  }
+  return layernorm_quant_common(p, x_dtype, num_items, num_slots, ld, ln_gamma, ln_beta, ln_dtype, eps, act_mode,
+                                static_scale, static_scale_dtype, q_out, ldq, scale_out, ln_out, stream);
 }

@@ -181,6 +181,34 @@ def layernorm_quant(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, ep
     return q, scale, ln
 
 
+def layernorm_quant_slots(slot_rows: Sequence[torch.Tensor], gamma: torch.Tensor, beta: torch.Tensor, eps: float,
+                          act_mode: str = "dynamic", static_scale: Optional[torch.Tensor] = None,
+                          want_ln: bool = False):
+    """LayerNorm (+ int8) of rows whose slot s is the [N, 512] view slot_rows[s] (common row stride)."""
+    dev = require_cuda("layernorm_quant_slots", gamma, beta, *slot_rows)
+    S = len(slot_rows)
+    n = slot_rows[0].shape[0]
+    ld = slot_rows[0].stride(0)
+    for v in slot_rows:
+        if tuple(v.shape) != (n, 512) or v.stride() != (ld, 1) or v.dtype != slot_rows[0].dtype:
+            raise ValueError("slot rows must be [N, 512] views with one common row stride and dtype")
+    H = S * 512
+    mode = {"dynamic": L.RB_ACT_DYNAMIC, "static": L.RB_ACT_STATIC, "none": L.RB_ACT_NONE}[act_mode]
+    q = torch.empty((n, H), dtype=torch.int8, device=dev) if mode != L.RB_ACT_NONE else None
+    scale = torch.empty((n,), dtype=torch.float32, device=dev) if mode == L.RB_ACT_DYNAMIC else None
+    ln = torch.empty((n, H), dtype=slot_rows[0].dtype, device=dev) if (want_ln or mode == L.RB_ACT_NONE) else None
+    gamma = _affine_f32(gamma)
+    beta = _affine_f32(beta)
+    if static_scale is not None:
+        static_scale = static_scale.contiguous()
+    with torch.cuda.device(dev):
+        L.call("rb_layernorm_quant_slots", L.ptr_array([v.data_ptr() for v in slot_rows]), rb_dtype(slot_rows[0]),
+               n, S, ld, gamma.data_ptr(), beta.data_ptr(), rb_dtype(gamma), float(eps), mode, _ptr(static_scale),
+               rb_dtype(static_scale) if static_scale is not None else 0, _ptr(q), H, _ptr(scale), _ptr(ln),
+               _stream(dev))
+    return q, scale, ln
+
+
 # ------------------------------------------------------------- quantisers
 def quant_dynamic_per_token_out(x2d: torch.Tensor, xq: torch.Tensor, scale: torch.Tensor):
     dev = require_cuda("dynamic_per_token_quantize_activation", x2d, xq, scale)

@@ -68,11 +68,11 @@ def _quantized_weight(rep: nn.Module):
 
 
 def rep_encoder_forward(rep: nn.Module, batch, act_mode: Optional[str] = None,
-                        return_intermediates: bool = False):
+                        return_intermediates: bool = False, out: Optional[torch.Tensor] = None):
     """Fused B200 forward of a RepEncoder-shaped module on a reference batch dict.
 
-    Returns rep_emb [N, d_model] in the table dtype (and, with
-    return_intermediates, a dict with q, scale, pooled and ln)."""
+    Returns rep_emb [N, d_model] in the table dtype (written into ``out`` when
+    given), and with return_intermediates a dict with q, scale, pooled and ln."""
     table = rep.emb.weight
     device = table.device
     if device.type != "cuda":
@@ -92,7 +92,10 @@ def rep_encoder_forward(rep: nn.Module, batch, act_mode: Optional[str] = None,
         table.detach(), values, offsets, ln.weight.detach(), ln.bias.detach(), ln.eps, act_mode=act_mode,
         static_scale=static_scale, want_pooled=return_intermediates, want_ln=return_intermediates)
     n = q.shape[0]
-    out = torch.empty((n, w_nk.shape[0]), dtype=table.dtype, device=device)
+    if out is None:
+        out = torch.empty((n, w_nk.shape[0]), dtype=table.dtype, device=device)
+    elif tuple(out.shape) != (n, w_nk.shape[0]) or out.dtype != table.dtype:
+        raise ValueError(f"out must be [{n}, {w_nk.shape[0]}] {table.dtype}")
     sa = scale if act_mode == "dynamic" else static_scale
     device_ops.w8a8_gemm(q, w_nk, sa, w_scale, out, bias=None if bias is None else bias.detach(),
                          sa_per_row=(act_mode == "dynamic"))

@@ -108,6 +108,17 @@ int rb_layernorm_quant(const void* x, int x_dtype, int64_t num_items, int num_sl
                        int act_mode, const void* static_scale, int static_scale_dtype,
                        int8_t* q_out, int64_t ldq, float* scale_out, void* ln_out, void* stream);
 
+/*
+ * rb_layernorm_quant with each slot's 512 columns read from its own place:
+ * slot s of item i at slot_rows[s] + i*ld (elements).  Lets the slot-sharded
+ * multi-GPU path normalise the rows it received from every rank in place
+ * (models.py:39-45 concat + LayerNorm, without materialising the concat).
+ */
+int rb_layernorm_quant_slots(const void* const* slot_rows, int x_dtype, int64_t num_items, int num_slots,
+                             int64_t ld, const void* ln_gamma, const void* ln_beta, int ln_dtype, float eps,
+                             int act_mode, const void* static_scale, int static_scale_dtype, int8_t* q_out,
+                             int64_t ldq, float* scale_out, void* ln_out, void* stream);
+
 /* quantization/w8a8_triton_kernels.py:41-64,392-422 dynamic_per_token_quantize_activation[_out]:
  * x[M,K] (row stride ldx elements) -> q[M,K] (row stride ldq), scale[M] fp32. */
 int rb_quant_dynamic_per_token(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,

@@ -171,3 +171,62 @@ def test_static_quantised_checkpoint_layer(cuda_device):
     acc = torch._int_mm(inter["q"], qw.qweight_t)
     ref = ((acc.float() * s) * lin.weight_scale.float()[None, :] + lin.bias.float()).to(torch.bfloat16)
     assert torch.equal(out, ref)
+
+
+def test_host_pipeline_matches_direct_forward(cuda_device):
+    """HostPipeline (overlapped H2D / forward / D2H) returns exactly the direct forward's output."""
+    import torch
+    from baidu_cti_grab_b200 import synth
+    from baidu_cti_grab_b200.pipeline import HostPipeline, pack_batch
+    from baidu_cti_grab_b200.rep_encoder import rep_encoder_forward
+
+    rep, _, _ = _setup(torch, cuda_device, users=4, seed=26)
+    cfg = synth.WorkloadConfig("pipe", 2000, "bfloat16", 40, 1, 90, "1+poisson1", 1.1)
+    host = [synth.make_batch(cfg, seed=100 + i) for i in range(5)]
+    packed = [pack_batch(b) for b in host]
+    outs = [torch.empty((pb.num_items, 512), dtype=torch.bfloat16).pin_memory() for pb in packed]
+    pipe = HostPipeline(rep, max_ids=max(sum(pb.lengths[:28]) for pb in packed),
+                        max_items=max(pb.num_items for pb in packed))
+    pipe.run(packed, outs)
+    pipe.synchronize()
+    for b, o in zip(host, outs):
+        dev_b = {s: (torch.from_numpy(b[s][0]).to(cuda_device), torch.from_numpy(b[s][1]).to(cuda_device))
+                 for s in range(1, 29)}
+        ref = rep_encoder_forward(rep, dev_b)
+        assert torch.equal(o, ref.cpu())
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_slot_sharded_path_emulated_on_one_gpu(cuda_device, world):
+    """The slot-sharded path (pool own slots -> exchange -> per-slot LayerNorm/int8 -> GEMM)
+    with `world` ranks emulated in one process: the exchange is a copy between the
+    emulated ranks' buffers.  Every rank's rows equal the single-GPU fused forward."""
+    import torch
+    from baidu_cti_grab_b200 import sharding, device_ops, synth
+    from baidu_cti_grab_b200.rep_encoder import rep_encoder_forward
+
+    R = 300
+    cfg = synth.WorkloadConfig("sharded", R, "bfloat16", 24, 1, 60, "1+poisson1", 1.2)
+    b = synth.make_batch(cfg, seed=31)
+    table = synth.make_table_torch(cfg.num_rows, seed=31, device=cuda_device)
+    rep, _, _ = _setup(torch, cuda_device, users=2, seed=31)
+    rep.emb.weight = torch.nn.Parameter(table, requires_grad=False)
+    values = [torch.from_numpy(b[s][0]).to(cuda_device) for s in range(1, 29)]
+    offsets = [torch.from_numpy(b[s][1]).to(cuda_device) for s in range(1, 29)]
+    full = rep_encoder_forward(rep, {s: (values[s - 1], offsets[s - 1]) for s in range(1, 29)})
+    w_nk, w_scale = rep._b200_wcache[1], rep._b200_wcache[2]
+    plans = [sharding.make_slot_plan(r, world, b["user_offsets"]) for r in range(world)]
+    encs = [sharding.SlotShardedRepEncoder(p, sharding.build_local_table(table, p, R), R, rep.input_norm.weight,
+                                           rep.input_norm.bias, 1e-5, w_nk, w_scale, rep.linear.bias,
+                                           all_to_all=lambda *a: None) for p in plans]
+    pooled = [e.pool_local(values, offsets) for e in encs]
+    for r, e in enumerate(encs):
+        def fake_a2a(out, inp, out_splits, in_splits, r=r):
+            i0, i1 = plans[r].my_items
+            mine = i1 - i0
+            for j in range(world):
+                out[j * mine:(j + 1) * mine].copy_(pooled[j][i0:i1])
+        e.all_to_all = fake_a2a
+        got = e.finish(pooled[r])
+        i0, i1 = plans[r].my_items
+        assert torch.equal(got, full[i0:i1])
