@@ -21,8 +21,11 @@
 namespace rb {
 
 constexpr int kSlotsPerWarp = 4;
+#ifndef RB_K1_SCALAR_LN
+#define RB_K1_SCALAR_LN 0  // 1: pass 2/3 in scalar fp32 instead of packed f32x2 (same results)
+#endif
 #ifndef RB_K1_BF16_ROWS
-#define RB_K1_BF16_ROWS 3
+#define RB_K1_BF16_ROWS 2
 #endif
 constexpr int kDim = 512;
 
@@ -277,7 +280,7 @@ __device__ __forceinline__ V sel4(const V* a, int j) {
 // to the row dtype, written back in place) with the absmax, and the int8
 // quantiser.  bf16 rows stay packed in shared memory (28 KB per item) and
 // enter fp32 arithmetic through the mixed-precision add/sub.
-template <typename T, int MODE>
+template <typename T, int MODE, bool kFull4>
 __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant__ RepParams p) {
   constexpr bool kBf16 = sizeof(T) == 2;
   constexpr int kRows = kBf16 ? RB_K1_BF16_ROWS : 2;  // table rows a warp holds in registers
@@ -293,7 +296,9 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
   const int64_t item = blockIdx.x;
   const int S = p.num_slots;
   const int slot0 = warp * kSlotsPerWarp;
-  const int nsl = max(0, min(kSlotsPerWarp, S - slot0));
+  // kFull4: every warp owns exactly four slots (S % 4 == 0, e.g. the 28-slot
+  // RepEncoder), so the per-slot loops unroll with constant offsets
+  const int nsl = kFull4 ? kSlotsPerWarp : max(0, min(kSlotsPerWarp, S - slot0));
 
   // pooled slot s of this warp is final in `acc` (fp32, not yet rounded):
   // round to T, keep it in shared memory, return the lane's first-pass partial
@@ -346,6 +351,7 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
   };
 
   if constexpr (MODE == kDenseLnQuant) {
+#pragma unroll
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
       const T* xseg = reinterpret_cast<const T*>(p.xs[s]) + item * p.ldx;
@@ -413,6 +419,7 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
     int w0 = 0;
     int my_id = load_window(0);
 
+#pragma unroll
     for (int j = 0; j < nsl; ++j) {
       const int tend = pre[j + 1];
       float acc[16];
@@ -481,17 +488,29 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
     // ---- pass 2: variance around the mean
 #pragma unroll
     for (int jj = 0; jj < kSlotsPerWarp; ++jj) part[jj] = 0.0f;
+#pragma unroll
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
       F2 a = f2(0.0f, 0.0f);
       if constexpr (kBf16) {
         uint32_t w[8];
         ld_words(s_words + s * 256, lane, w);
+#if RB_K1_SCALAR_LN
+        float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float d0 = sub_lo(w[i], mean), d1 = sub_hi(w[i], mean);
+          a0 = __fmaf_rn(d0, d0, a0);
+          a1 = __fmaf_rn(d1, d1, a1);
+        }
+        a = f2(a0, a1);
+#else
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const F2 d = f2(sub_lo(w[i], mean), sub_hi(w[i], mean));
           a = fma2(d, d, a);
         }
+#endif
       } else {
         F2 x[8];
         lds_pairs(s_f32, s, lane, x);
@@ -517,6 +536,7 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
     const F2 rstd2 = f2(rstd, rstd);
     // ---- pass 3: y = fma(rstd * (x - mean), gamma, beta) rounded to T, in place; absmax
     float amax = 0.0f;
+#pragma unroll
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
       F2 g[8], b[8], y[8];
@@ -528,8 +548,14 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
         ld_words(s_words + s * 256, lane, w);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
+#if RB_K1_SCALAR_LN
+          const float2 gg = un(g[i]), bb = un(b[i]);
+          const float2 v = make_float2(__fmaf_rn(__fmul_rn(rstd, sub_lo(w[i], mean)), gg.x, bb.x),
+                                       __fmaf_rn(__fmul_rn(rstd, sub_hi(w[i], mean)), gg.y, bb.y));
+#else
           const F2 d = f2(sub_lo(w[i], mean), sub_hi(w[i], mean));
           const float2 v = un(fma2(mul2(rstd2, d), g[i], b[i]));
+#endif
           // rounding to bf16 is monotonic and symmetric, so the absmax of the
           // rounded row is the rounded absmax of the fp32 row
           amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
@@ -574,6 +600,7 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
     const F2 inv2 = f2(inv, inv);
     const bool clamp = p.act_mode == RB_ACT_STATIC;
     // ---- pass 4: int8 = clamp(round_half_away(y * inv), -128, 127)
+#pragma unroll
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
       F2 x[8];
@@ -639,16 +666,12 @@ static int launch_rep(const RepParams& p, int row_dtype, cudaStream_t stream) {
   // the item's pooled row: packed bf16, or fp32 for fp32 tables
   const size_t smem = (size_t)p.num_slots * kDim * dtype_size(row_dtype);
   cudaError_t e = cudaSuccess;
-  if (row_dtype == RB_BF16) {
-    if (smem > 48 * 1024)
-      e = cudaFuncSetAttribute(rep_fused_kernel<__nv_bfloat16, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem);
-    if (e == cudaSuccess) rep_fused_kernel<__nv_bfloat16, MODE><<<grid, block, smem, stream>>>(p);
-  } else {
-    if (smem > 48 * 1024)
-      e = cudaFuncSetAttribute(rep_fused_kernel<float, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess) rep_fused_kernel<float, MODE><<<grid, block, smem, stream>>>(p);
-  }
+  const bool full4 = p.num_slots % kSlotsPerWarp == 0;
+  auto kern = row_dtype == RB_BF16
+                  ? (full4 ? rep_fused_kernel<__nv_bfloat16, MODE, true> : rep_fused_kernel<__nv_bfloat16, MODE, false>)
+                  : (full4 ? rep_fused_kernel<float, MODE, true> : rep_fused_kernel<float, MODE, false>);
+  if (smem > 48 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) kern<<<grid, block, smem, stream>>>(p);
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(rep_fused_kernel)");
   return check_cuda(cudaGetLastError(), "rep_fused_kernel launch");
 }
