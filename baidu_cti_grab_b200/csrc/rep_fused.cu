@@ -24,6 +24,9 @@ constexpr int kSlotsPerWarp = 4;
 #ifndef RB_K1_SCALAR_LN
 #define RB_K1_SCALAR_LN 0  // 1: pass 2/3 in scalar fp32 instead of packed f32x2 (same results)
 #endif
+#ifndef RB_K1_PAIR_ASM
+#define RB_K1_PAIR_ASM 0  // 1: build the bf16-minus-mean pairs inside one asm block
+#endif
 #ifndef RB_K1_BF16_ROWS
 #define RB_K1_BF16_ROWS 2
 #endif
@@ -174,6 +177,25 @@ __device__ __forceinline__ float sub_hi(uint32_t w, float m) {  // bf16(hi) - m
   return d;
 }
 
+// (w's two bf16 - m) as an fp32 pair, built inside one asm block so that the
+// two halves can be allocated straight into the pair register
+__device__ __forceinline__ F2 sub_pair(uint32_t w, float m) {
+  F2 d;
+  asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 a, b;\n\tmov.b32 {lo, hi}, %1;\n\t"
+      "sub.rn.f32.bf16 a, lo, %2;\n\tsub.rn.f32.bf16 b, hi, %2;\n\tmov.b64 %0, {a, b};\n\t}"
+      : "=l"(d.r) : "r"(w), "f"(m));
+  return d;
+}
+// acc += (w - m)^2 for both halves of w (packed fma)
+__device__ __forceinline__ F2 sq_acc(F2 acc, uint32_t w, float m) {
+  F2 d;
+  asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 a, b;\n\t.reg .b64 t;\n\tmov.b32 {lo, hi}, %1;\n\t"
+      "sub.rn.f32.bf16 a, lo, %2;\n\tsub.rn.f32.bf16 b, hi, %2;\n\tmov.b64 t, {a, b};\n\t"
+      "fma.rn.f32x2 %0, t, t, %3;\n\t}"
+      : "=l"(d.r) : "r"(w), "f"(m), "l"(acc.r));
+  return d;
+}
+
 // ------------------------------------------------ row pieces per element type
 // A lane's 16 values of a 512-wide slot segment are columns 8l..8l+7 and
 // 256+8l..256+8l+7.  bf16 rows travel as 8 packed words (w[i] = elements
@@ -285,9 +307,10 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
   constexpr bool kBf16 = sizeof(T) == 2;
   constexpr int kRows = kBf16 ? RB_K1_BF16_ROWS : 2;  // table rows a warp holds in registers
   extern __shared__ __align__(16) uint8_t s_raw[];
-  __shared__ float s_tot[RB_MAX_SLOTS];
+  __shared__ float s_tot[RB_MAX_SLOTS];  // per-slot sums T_s
+  __shared__ float s_q[RB_MAX_SLOTS];    // per-slot centred square sums Q_s
   __shared__ float s_wmax[8];
-  __shared__ float s_stat[4];  // mean, rstd, scale, inv
+  __shared__ float s_stat[2];  // mean, rstd
   uint32_t* s_words = reinterpret_cast<uint32_t*>(s_raw);  // bf16 row: 256 words per slot
   float* s_f32 = reinterpret_cast<float*>(s_raw);          // fp32 row: 512 floats per slot
 
@@ -343,11 +366,6 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
 #pragma unroll
     for (int jj = 0; jj < kSlotsPerWarp; ++jj)
       if (jj == j) part[jj] = v;
-  };
-  auto reduce_parts = [&]() {
-    const float t = warp_sum4_butterfly(part[0], part[1], part[2], part[3], lane);
-    const int j = lane >> 3;
-    if ((lane & 7) == 0 && j < nsl) s_tot[slot0 + j] = t;
   };
 
   if constexpr (MODE == kDenseLnQuant) {
@@ -474,64 +492,68 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
   }
 
   if constexpr (MODE != kGatherPool) {
-    reduce_parts();
     const float H = (float)(S * kDim);
+    // ---- per-slot statistics: T_s (sum), then Q_s = sum (x - T_s/512)^2
+    const float slot_sum = warp_sum4_butterfly(part[0], part[1], part[2], part[3], lane);  // lanes 8j..: slot j
+    float m_slot[kSlotsPerWarp];
+#pragma unroll
+    for (int j = 0; j < kSlotsPerWarp; ++j)
+      m_slot[j] = __fmul_rn(__shfl_sync(0xffffffffu, slot_sum, 8 * j), 0.001953125f);  // T_j / 512, exact
+#pragma unroll
+    for (int j = 0; j < kSlotsPerWarp; ++j) {
+      float q = 0.0f;
+      if (j < nsl) {
+        const int s = slot0 + j;
+        F2 a = f2(0.0f, 0.0f);
+        if constexpr (kBf16) {
+          uint32_t w[8];
+          ld_words(s_words + s * 256, lane, w);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const F2 d = f2(sub_lo(w[i], m_slot[j]), sub_hi(w[i], m_slot[j]));
+            a = fma2(d, d, a);
+          }
+        } else {
+          F2 x[8];
+          lds_pairs(s_f32, s, lane, x);
+          const F2 m2 = f2(m_slot[j], m_slot[j]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const F2 d = sub2(x[i], m2);
+            a = fma2(d, d, a);
+          }
+        }
+        const float2 v = un(a);
+        q = __fadd_rn(v.x, v.y);
+      }
+      part[j] = q;
+    }
+    const float slot_q = warp_sum4_butterfly(part[0], part[1], part[2], part[3], lane);
+    {
+      const int j = lane >> 3;
+      if ((lane & 7) == 0 && j < nsl) {
+        s_tot[slot0 + j] = slot_sum;
+        s_q[slot0 + j] = slot_q;
+      }
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
+      // combine the slots in slot order (Chan's parallel variance update)
       float t = 0.0f;
       for (int s = 0; s < S; ++s) t = __fadd_rn(t, s_tot[s]);
-      s_stat[0] = __fdiv_rn(t, H);
+      const float mean = __fdiv_rn(t, H);
+      float m2 = 0.0f;
+      for (int s = 0; s < S; ++s) {
+        const float d = __fsub_rn(__fmul_rn(s_tot[s], 0.001953125f), mean);
+        m2 = __fadd_rn(m2, __fadd_rn(s_q[s], __fmul_rn(512.0f, __fmul_rn(d, d))));
+      }
+      const float var = __fdiv_rn(m2, H);
+      s_stat[0] = mean;
+      s_stat[1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
     }
     __syncthreads();
     const float mean = s_stat[0];
     const F2 mean2 = f2(mean, mean);
-    // ---- pass 2: variance around the mean
-#pragma unroll
-    for (int jj = 0; jj < kSlotsPerWarp; ++jj) part[jj] = 0.0f;
-#pragma unroll
-    for (int j = 0; j < nsl; ++j) {
-      const int s = slot0 + j;
-      F2 a = f2(0.0f, 0.0f);
-      if constexpr (kBf16) {
-        uint32_t w[8];
-        ld_words(s_words + s * 256, lane, w);
-#if RB_K1_SCALAR_LN
-        float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float d0 = sub_lo(w[i], mean), d1 = sub_hi(w[i], mean);
-          a0 = __fmaf_rn(d0, d0, a0);
-          a1 = __fmaf_rn(d1, d1, a1);
-        }
-        a = f2(a0, a1);
-#else
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const F2 d = f2(sub_lo(w[i], mean), sub_hi(w[i], mean));
-          a = fma2(d, d, a);
-        }
-#endif
-      } else {
-        F2 x[8];
-        lds_pairs(s_f32, s, lane, x);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const F2 d = sub2(x[i], mean2);
-          a = fma2(d, d, a);
-        }
-      }
-      const float2 v = un(a);
-      put_part(j, __fadd_rn(v.x, v.y));
-    }
-    reduce_parts();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float t = 0.0f;
-      for (int s = 0; s < S; ++s) t = __fadd_rn(t, s_tot[s]);
-      const float var = __fdiv_rn(t, H);
-      s_stat[1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
-    }
-    __syncthreads();
     const float rstd = s_stat[1];
     const F2 rstd2 = f2(rstd, rstd);
     // ---- pass 3: y = fma(rstd * (x - mean), gamma, beta) rounded to T, in place; absmax
@@ -552,6 +574,8 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
           const float2 gg = un(g[i]), bb = un(b[i]);
           const float2 v = make_float2(__fmaf_rn(__fmul_rn(rstd, sub_lo(w[i], mean)), gg.x, bb.x),
                                        __fmaf_rn(__fmul_rn(rstd, sub_hi(w[i], mean)), gg.y, bb.y));
+#elif RB_K1_PAIR_ASM
+          const float2 v = un(fma2(mul2(rstd2, sub_pair(w[i], mean)), g[i], b[i]));
 #else
           const F2 d = f2(sub_lo(w[i], mean), sub_hi(w[i], mean));
           const float2 v = un(fma2(mul2(rstd2, d), g[i], b[i]));
@@ -582,21 +606,17 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
     amax = warp_max(amax);
     if (lane == 0) s_wmax[warp] = amax;
     __syncthreads();
-    if (threadIdx.x == 0) {
-      float inv;
-      if (p.act_mode == RB_ACT_DYNAMIC) {
-        float m = 0.0f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, s_wmax[w]);
-        m = fmaxf(m, 1e-8f);
-        p.scale[item] = __fdiv_rn(m, 127.0f);
-        inv = __fdiv_rn(127.0f, m);
-      } else {
-        inv = __fdiv_rn(1.0f, load_as_f32(p.static_scale, p.static_scale_dtype, 0));
-      }
-      s_stat[3] = inv;
+    // every thread derives the quantiser scale (no second barrier)
+    float inv;
+    if (p.act_mode == RB_ACT_DYNAMIC) {
+      float m = 0.0f;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, s_wmax[w]);
+      m = fmaxf(m, 1e-8f);
+      inv = __fdiv_rn(127.0f, m);
+      if (threadIdx.x == 0) p.scale[item] = __fdiv_rn(m, 127.0f);
+    } else {
+      inv = __fdiv_rn(1.0f, load_as_f32(p.static_scale, p.static_scale_dtype, 0));
     }
-    __syncthreads();
-    const float inv = s_stat[3];
     const F2 inv2 = f2(inv, inv);
     const bool clamp = p.act_mode == RB_ACT_STATIC;
     // ---- pass 4: int8 = clamp(round_half_away(y * inv), -128, 127)

@@ -36,10 +36,13 @@
  * positions into a1 (both from 0.0f), and the lane partial is a0 + a1; the
  * 32 lane partials are combined by an xor-butterfly with distances 16, 8, 4,
  * 2, 1 (p[l] = p[l] + p[l^d]); the slot totals are then added in slot order
- * starting from 0.0f.  The first pass sums x, the second pass sums
- * (x - mean)^2 with fmaf(d, d, acc).  (The even/odd split is what a packed
- * two-wide fp32 add computes.)
- *   mean = total1 / H;  var = total2 / H;  rstd = 1.0f / sqrtf(var + eps)
+ * starting from 0.0f.  (The even/odd split is what a packed two-wide fp32
+ * add computes.)  Per slot s this order gives the sum T_s of x and, with the
+ * slot mean m_s = T_s / 512, the centred square sum Q_s of (x - m_s)^2
+ * (fmaf(d, d, acc) per element).  The slots are then combined in slot order:
+ *   mean = (sum_s T_s) / H
+ *   M2   = sum_s (Q_s + 512 * (m_s - mean)^2)       (Chan's parallel update)
+ *   var  = M2 / H;  rstd = 1.0f / sqrtf(var + eps)
  *   y    = fmaf(rstd * (x - mean), gamma, beta)   (then RNE to the row dtype)
  * Division and square root are IEEE correctly rounded here and in the kernel.
  */
@@ -208,12 +211,22 @@ void rbo_layernorm_row(const float* x, int64_t n_slots, const float* gamma, cons
                        float eps, int out_dtype, float* y, float* mean_out, float* rstd_out) {
     const int64_t H = n_slots * 512;
     float t1 = 0.0f;
-    for (int64_t s = 0; s < n_slots; ++s) t1 = t1 + canonical_slot_sum(x + s * 512, 0.0f, 0);
-    float mean = t1 / (float)H;
-    float t2 = 0.0f;
-    for (int64_t s = 0; s < n_slots; ++s) t2 = t2 + canonical_slot_sum(x + s * 512, mean, 1);
-    float var = t2 / (float)H;
-    float rstd = 1.0f / sqrtf(var + eps);
+    float slot_sum[64], slot_q[64];
+    for (int64_t s = 0; s < n_slots; ++s) {
+        slot_sum[s] = canonical_slot_sum(x + s * 512, 0.0f, 0);
+        const float m_s = slot_sum[s] / 512.0f;
+        slot_q[s] = canonical_slot_sum(x + s * 512, m_s, 1);
+        t1 = t1 + slot_sum[s];
+    }
+    const float mean = t1 / (float)H;
+    /* Chan's combination of the per-slot centred sums, in slot order */
+    float m2 = 0.0f;
+    for (int64_t s = 0; s < n_slots; ++s) {
+        const float d = slot_sum[s] / 512.0f - mean;
+        m2 = m2 + (slot_q[s] + 512.0f * (d * d));
+    }
+    const float var = m2 / (float)H;
+    const float rstd = 1.0f / sqrtf(var + eps);
     for (int64_t k = 0; k < H; ++k) {
         float d = x[k] - mean;
         float t = rstd * d;
