@@ -32,6 +32,11 @@
 
 #include "common.cuh"
 
+// smallest M that uses the two-SM kernel (below it the one-SM kernel fills more SMs)
+#ifndef RB_GEMM_PAIR_MIN_M
+#define RB_GEMM_PAIR_MIN_M 1024
+#endif
+
 namespace rb {
 namespace tc {
 
@@ -352,6 +357,243 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ----------------------------------------------------------------------------
+// Two-SM variant (cta_group::2): a cluster of two CTAs computes a 256x256 tile
+// with one tcgen05.mma.cta_group::2 (M=256, N=256, K=32) per K step.  CTA r of
+// the pair loads A rows [r*128, r*128+128) and B rows (N) [r*128, r*128+128)
+// of the tile into its own shared memory; the MMA, issued by the leader (rank
+// 0), reads both CTAs' halves, so each SM's tensor core reads 8 KB of operands
+// per 128-clock MMA instead of 12 KB, and TMA writes drop by a third.  Each
+// CTA's TMEM holds its own 128 output rows (two 256-column buffers, so the
+// epilogue overlaps the next tile).  Loads carry no multicast: every CTA
+// fetches its own halves; the leader's full barrier counts both CTAs' bytes.
+namespace pair {
+constexpr int BM = 256;  // rows per tile (128 per CTA)
+constexpr int BN = 256;
+constexpr int BK = 128;  // K bytes per stage
+constexpr int STAGES = 6;
+constexpr int A_BYTES = 128 * BK;  // this CTA's A half
+constexpr int B_BYTES = 128 * BK;  // this CTA's B half
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 512;
+constexpr int NUM_THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                           ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* tm, int c0, int c1, uint32_t bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
+      "r"(0u));
+}
+// arrive on the barrier at this shared offset in both CTAs of the pair when the MMAs issued so far are done
+__device__ __forceinline__ void umma_commit_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    w8a8_gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ EpiParams ep) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;                // [STAGES]  leader: TMA bytes of both CTAs -> MMA
+  uint64_t* empty = bars + STAGES;      // [STAGES]  both: MMA done with the slot -> TMA
+  uint64_t* tfull = bars + 2 * STAGES;  // [2]       both: accumulator ready -> epilogue
+  uint64_t* tempty = tfull + 2;         // [2]       leader: both epilogues done -> MMA
+  uint64_t* done = tempty + 2;          // [1]       leader: all MMAs complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&tfull[b]), 1);
+      mbar_init(smem_u32(&tempty[b]), 2 * 4);  // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(smem_u32(done), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int64_t m_tiles = (ep.M + BM - 1) / BM;
+  const int64_t n_tiles = (ep.N + BN - 1) / BN;
+  const int64_t num_tiles = m_tiles * n_tiles;
+  const int kblocks = (int)((ep.K + BK - 1) / BK);
+  const int64_t pair_id = blockIdx.x >> 1;
+  const int64_t num_pairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      const uint64_t pol_a = policy_evict_first(), pol_b = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, issued_phase = 0;
+      bool ok = true;
+      for (int64_t tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+        const int m0 = (int)((tile / n_tiles) * BM) + (int)rank * 128;
+        const int n0 = (int)((tile % n_tiles) * BN) + (int)rank * 128;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, kWaitTimeoutProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb_local = smem_u32(&full[stage]);
+          if (leader) mbar_arrive_expect_tx(fb_local, 2 * STAGE_BYTES);
+          const uint32_t fb = map_rank(fb_local, 0);
+          tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), &tmA, kb * BK, m0, fb, pol_a);
+          tma_load_2d_pair(smem_u32(sB + stage * B_BYTES), &tmB, kb * BK, n0, fb, pol_b);
+          issued |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (leader) {
+        // the leader's full barriers count both CTAs' bytes: drain them before exit
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s))
+            mbar_wait_bounded(smem_u32(&full[s]), (issued_phase >> s) & 1u, kWaitTimeoutProducer, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // --------------------------------------------------------------- MMA
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int64_t tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+        if (!mbar_wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1, kWaitTimeoutMma, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&full[stage]), phase, kWaitTimeoutMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = sw128_desc(smem_u32(sA + stage * A_BYTES));
+          const uint64_t bdesc = sw128_desc(smem_u32(sB + stage * B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / MMA_K; ++k)
+            umma_i8_pair(d_tmem, adesc + (uint64_t)(k * MMA_K / 16), bdesc + (uint64_t)(k * MMA_K / 16),
+                         (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_both(smem_u32(&empty[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_both(smem_u32(&tfull[acc]));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       smem_u32(done))
+                   : "memory");
+      mbar_wait_bounded(smem_u32(done), 0, kWaitTimeoutMma, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const uint32_t tempty_leader[2] = {map_rank(smem_u32(&tempty[0]), 0), map_rank(smem_u32(&tempty[1]), 0)};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
+      const int64_t m0 = (tile / n_tiles) * BM + (int64_t)rank * 128;
+      const int64_t n0 = (tile % n_tiles) * BN;
+      if (!mbar_wait_bounded(smem_u32(&tfull[acc]), acc_phase, kWaitTimeoutEpilogue, abort_flag)) break;
+      tc_fence_after();
+      const int64_t row = m0 + quarter * 32 + lane;
+      float sa_v = 0.0f;
+      if (row < ep.M && ep.out_dtype != RB_I32) sa_v = load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? row : 0);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int64_t col0 = n0 + c * 32;
+        if (col0 >= ep.N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+        if (row < ep.M) epilogue_32(r, row, col0, sa_v, ep);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty_leader[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+}  // namespace pair
+
 // CUDA-core GEMM for shapes the tensor-map path cannot take (K % 16 != 0,
 // unaligned operands, K == 0).  One thread per output element.
 __global__ void w8a8_gemm_simple_kernel(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
@@ -411,6 +653,7 @@ static int make_tmap(CUtensorMap* tm, const int8_t* base, int64_t inner, int64_t
 }
 
 static std::once_flag g_attr_once[64];
+static std::once_flag g_pair_attr_once[64];
 
 }  // namespace tc
 }  // namespace rb
@@ -472,6 +715,38 @@ extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64
     attr_err = cudaFuncSetAttribute(w8a8_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return check_cuda(attr_err, "cudaFuncSetAttribute(w8a8_gemm_tc_kernel)");
+  if (M >= RB_GEMM_PAIR_MIN_M) {
+    // two-SM tiles: each CTA of a pair loads 128 rows of A and 128 of B
+    CUtensorMap tpA, tpB;
+    rc = make_tmap(&tpA, A, K, M, lda, pair::BK, 128);
+    if (rc) return rc;
+    rc = make_tmap(&tpB, B, K, N, ldb, pair::BK, 128);
+    if (rc) return rc;
+    cudaError_t pe = cudaSuccess;
+    std::call_once(g_pair_attr_once[dev & 63], [&] {
+      pe = cudaFuncSetAttribute(pair::w8a8_gemm_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                pair::SMEM_BYTES);
+      if (pe == cudaSuccess)
+        pe = cudaFuncSetAttribute(pair::w8a8_gemm_tc_pair_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+    });
+    if (pe != cudaSuccess) return check_cuda(pe, "cudaFuncSetAttribute(w8a8_gemm_tc_pair_kernel)");
+    const int64_t ptiles = ((M + pair::BM - 1) / pair::BM) * ((N + pair::BN - 1) / pair::BN);
+    const int pairs = (int)std::min<int64_t>(ptiles, sm_count() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(pair::NUM_THREADS);
+    cfg.dynamicSmemBytes = pair::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, pair::w8a8_gemm_tc_pair_kernel, tpA, tpB, ep),
+                      "w8a8_gemm_tc_pair_kernel launch");
+  }
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = (int)std::min<int64_t>(tiles, sm_count());
   w8a8_gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tmA, tmB, ep);
