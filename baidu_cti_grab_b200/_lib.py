@@ -42,11 +42,16 @@ SIGNATURES = {
     "rb_pack_weight_nk": [_vp, _i64, _i64, _i64, _i64, _vp, _vp],
     "rb_w8a8_gemm": [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp, _i32, _vp,
                      _i64, _i32, _vp],
+    "rb_w8a8_gemm_ws": [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp, _i32, _vp,
+                        _i64, _i32, _vp, _i64, _vp],
+    "rb_w8a8_gemm_workspace_size": [_i64, _i64, _i64],
     "rb_device_supported": [],
     "rb_device_error": [_i32],
     "rb_selftest_wait_timeout": [_u64, _vp],
     "rb_version": [],
 }
+
+RETURNS_I64 = {"rb_w8a8_gemm_workspace_size"}
 
 _lock = threading.Lock()
 _lib: Optional[ctypes.CDLL] = None
@@ -73,7 +78,7 @@ def load() -> ctypes.CDLL:
         for name, argtypes in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.argtypes = argtypes
-            fn.restype = ctypes.c_int
+            fn.restype = ctypes.c_int64 if name in RETURNS_I64 else ctypes.c_int
         lib.rb_last_error.argtypes = []
         lib.rb_last_error.restype = ctypes.c_char_p
         _lib = lib

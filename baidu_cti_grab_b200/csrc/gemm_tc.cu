@@ -32,9 +32,11 @@
 
 #include "common.cuh"
 
-// smallest M that uses the two-SM kernel (below it the one-SM kernel fills more SMs)
+// smallest M that uses the two-SM kernel: 256-row pair tiles must fill about
+// two waves of the 74 CTA pairs; below it the one-SM kernel, split along K,
+// spreads the work over all SMs
 #ifndef RB_GEMM_PAIR_MIN_M
-#define RB_GEMM_PAIR_MIN_M 1024
+#define RB_GEMM_PAIR_MIN_M 16384
 #endif
 
 namespace rb {
@@ -67,6 +69,8 @@ struct EpiParams {
   int64_t ldo;
   int64_t M, N, K;
   int sa_dtype, sa_per_row, sb_dtype, bias_dtype, out_dtype;
+  int ksplits;         // > 1: each tile covers a K range and writes raw int32 partials
+  int32_t* partials;   // [ksplits][M][N] int32 when ksplits > 1
 };
 
 // K-major operand tile in shared memory with 128-byte swizzle: rows of 128 B,
@@ -247,8 +251,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int64_t m_tiles = (ep.M + BM - 1) / BM;
   const int64_t n_tiles = (ep.N + BN - 1) / BN;
-  const int64_t num_tiles = m_tiles * n_tiles;
+  const int ksplits = ep.ksplits;
+  const int64_t num_tiles = m_tiles * n_tiles * ksplits;
   const int kblocks = (int)((ep.K + BK - 1) / BK);
+  // tile t -> split t % ksplits, n tile (t / ksplits) % n_tiles, m tile t / (ksplits * n_tiles);
+  // split s covers k blocks [s*kblocks/ksplits, (s+1)*kblocks/ksplits)
+  auto kb_begin = [&](int64_t t) { return (int)((t % ksplits) * kblocks / ksplits); };
+  auto kb_end = [&](int64_t t) { return (int)((t % ksplits + 1) * kblocks / ksplits); };
+  auto tile_m0 = [&](int64_t t) { return (t / ksplits / n_tiles) * BM; };
+  auto tile_n0 = [&](int64_t t) { return ((t / ksplits) % n_tiles) * BN; };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -258,9 +269,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0, issued = 0, issued_phase = 0;
       bool ok = true;
       for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (int)((tile / n_tiles) * BM);
-        const int n0 = (int)((tile % n_tiles) * BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int m0 = (int)tile_m0(tile);
+        const int n0 = (int)tile_n0(tile);
+        for (int kb = kb_begin(tile); kb < kb_end(tile); ++kb) {
           if (!mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, kWaitTimeoutProducer, abort_flag)) {
             ok = false;
             break;
@@ -292,7 +303,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!mbar_wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1, kWaitTimeoutMma, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int kb0 = kb_begin(tile);
+        for (int kb = kb0; kb < kb_end(tile); ++kb) {
           if (!mbar_wait_bounded(smem_u32(&full[stage]), phase, kWaitTimeoutMma, abort_flag)) {
             ok = false;
             break;
@@ -303,7 +315,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / MMA_K; ++k)
             umma_i8(d_tmem, adesc + (uint64_t)(k * MMA_K / 16), bdesc + (uint64_t)(k * MMA_K / 16),
-                    (kb > 0 || k > 0) ? 1u : 0u);
+                    (kb > kb0 || k > 0) ? 1u : 0u);
           umma_commit(smem_u32(&empty[stage]));
           if (++stage == STAGES) {
             stage = 0;
@@ -324,22 +336,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 are reachable from this warp
     int acc = 0;
     uint32_t acc_phase = 0;
+    // split-K tiles store raw int32 partials into their split's slab
+    EpiParams pep = ep;
+    pep.out_dtype = RB_I32;
+    pep.ldo = ep.N;
     for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int64_t m0 = (tile / n_tiles) * BM;
-      const int64_t n0 = (tile % n_tiles) * BN;
+      const int64_t m0 = tile_m0(tile);
+      const int64_t n0 = tile_n0(tile);
       if (!mbar_wait_bounded(smem_u32(&tfull[acc]), acc_phase, kWaitTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const int64_t row = m0 + quarter * 32 + lane;
       float sa_v = 0.0f;
-      if (row < ep.M && ep.out_dtype != RB_I32)
+      if (row < ep.M && ep.out_dtype != RB_I32 && ksplits == 1)
         sa_v = load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? row : 0);
+      if (ksplits > 1) pep.out = ep.partials + (tile % ksplits) * ep.M * ep.N;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int64_t col0 = n0 + c * 32;
         if (col0 >= ep.N) break;  // warp-uniform
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-        if (row < ep.M) epilogue_32(r, row, col0, sa_v, ep);
+        if (row < ep.M) epilogue_32(r, row, col0, sa_v, ksplits > 1 ? pep : ep);
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[acc]));
@@ -594,6 +611,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 }  // namespace pair
 
+// Split-K reduction: out[m,n] = epilogue(sum over splits s = 0..S-1 of the int32
+// partials, in split order).  int32 addition is exact, so the result equals the
+// unsplit GEMM's bit for bit.
+__global__ void splitk_finalize_kernel(const __grid_constant__ EpiParams ep) {
+  const int64_t total = ep.M * ep.N;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int32_t acc = 0;
+    for (int s = 0; s < ep.ksplits; ++s) acc += ep.partials[s * total + idx];
+    const int64_t m = idx / ep.N, n = idx % ep.N;
+    if (ep.out_dtype == RB_I32) {
+      reinterpret_cast<int32_t*>(ep.out)[m * ep.ldo + n] = acc;
+      continue;
+    }
+    float v = __int2float_rn(acc);
+    v = __fmul_rn(v, load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? m : 0));
+    v = __fmul_rn(v, load_as_f32(ep.sb, ep.sb_dtype, n));
+    if (ep.bias != nullptr) v = __fadd_rn(v, load_as_f32(ep.bias, ep.bias_dtype, n));
+    if (ep.out_dtype == RB_F32) {
+      reinterpret_cast<float*>(ep.out)[m * ep.ldo + n] = v;
+    } else if (ep.out_dtype == RB_BF16) {
+      reinterpret_cast<__nv_bfloat16*>(ep.out)[m * ep.ldo + n] = __float2bfloat16_rn(v);
+    } else {
+      reinterpret_cast<__half*>(ep.out)[m * ep.ldo + n] = __float2half_rn(v);
+    }
+  }
+}
+
 // CUDA-core GEMM for shapes the tensor-map path cannot take (K % 16 != 0,
 // unaligned operands, K == 0).  One thread per output element.
 __global__ void w8a8_gemm_simple_kernel(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
@@ -660,10 +705,27 @@ static std::once_flag g_pair_attr_once[64];
 
 using namespace rb;
 
-extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M, int64_t N,
-                            int64_t K, const void* sa, int sa_dtype, int sa_per_row, const void* sb, int sb_dtype,
-                            const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
-                            void* stream) {
+// split-K factor for the one-SM kernel (1 = no split): enough (m, n, k) tiles to
+// cover the SMs, at least two K blocks per split
+static int choose_ksplits(int64_t M, int64_t N, int64_t K) {
+  using namespace rb::tc;
+  if (M >= RB_GEMM_PAIR_MIN_M || K <= 0 || K % 16 != 0) return 1;
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int64_t kblocks = (K + BK - 1) / BK;
+  int64_t s = std::min<int64_t>(sm_count() / std::max<int64_t>(tiles, 1), kblocks / 2);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(s, 256));
+}
+
+extern "C" int64_t rb_w8a8_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0) return 0;
+  const int s = choose_ksplits(M, N, K);
+  return s > 1 ? (int64_t)s * M * N : 0;
+}
+
+extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M, int64_t N,
+                               int64_t K, const void* sa, int sa_dtype, int sa_per_row, const void* sb, int sb_dtype,
+                               const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
+                               int32_t* workspace, int64_t workspace_elems, void* stream) {
   using namespace rb::tc;
   if (M < 0 || N < 0 || K < 0) return fail(RB_ERR_VALUE, "negative GEMM shape");
   if (M == 0 || N == 0) return RB_OK;
@@ -692,6 +754,8 @@ extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64
   ep.sb_dtype = sb_dtype;
   ep.bias_dtype = bias_dtype;
   ep.out_dtype = out_dtype;
+  ep.ksplits = 1;
+  ep.partials = nullptr;
   cudaStream_t st = (cudaStream_t)stream;
 
   const bool tma_ok = K > 0 && K % 16 == 0 && lda % 16 == 0 && ldb % 16 == 0 && aligned(A, 16) &&
@@ -703,18 +767,9 @@ extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64
     w8a8_gemm_simple_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(A, lda, B, ldb, ep);
     return check_cuda(cudaGetLastError(), "w8a8_gemm_simple_kernel launch");
   }
-  CUtensorMap tmA, tmB;
-  int rc = make_tmap(&tmA, A, K, M, lda, BK, BM);
-  if (rc) return rc;
-  rc = make_tmap(&tmB, B, K, N, ldb, BK, BN);
-  if (rc) return rc;
   int dev = 0;
   cudaGetDevice(&dev);
-  cudaError_t attr_err = cudaSuccess;
-  std::call_once(g_attr_once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(w8a8_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  });
-  if (attr_err != cudaSuccess) return check_cuda(attr_err, "cudaFuncSetAttribute(w8a8_gemm_tc_kernel)");
+  int rc;
   if (M >= RB_GEMM_PAIR_MIN_M) {
     // two-SM tiles: each CTA of a pair loads 128 rows of A and 128 of B
     CUtensorMap tpA, tpB;
@@ -726,8 +781,6 @@ extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64
     std::call_once(g_pair_attr_once[dev & 63], [&] {
       pe = cudaFuncSetAttribute(pair::w8a8_gemm_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 pair::SMEM_BYTES);
-      if (pe == cudaSuccess)
-        pe = cudaFuncSetAttribute(pair::w8a8_gemm_tc_pair_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
     });
     if (pe != cudaSuccess) return check_cuda(pe, "cudaFuncSetAttribute(w8a8_gemm_tc_pair_kernel)");
     const int64_t ptiles = ((M + pair::BM - 1) / pair::BM) * ((N + pair::BN - 1) / pair::BN);
@@ -747,8 +800,41 @@ extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64
     return check_cuda(cudaLaunchKernelEx(&cfg, pair::w8a8_gemm_tc_pair_kernel, tpA, tpB, ep),
                       "w8a8_gemm_tc_pair_kernel launch");
   }
-  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  // one-SM tiles, split along K when the (m, n) tiles alone cannot fill the GPU
+  int ks = choose_ksplits(M, N, K);
+  if (ks > 1) {
+    if (workspace == nullptr || workspace_elems < (int64_t)ks * M * N) {
+      ks = 1;  // no (or too small a) workspace: run unsplit
+    } else {
+      ep.ksplits = ks;
+      ep.partials = workspace;
+    }
+  }
+  CUtensorMap tmA, tmB;
+  rc = make_tmap(&tmA, A, K, M, lda, BK, BM);
+  if (rc) return rc;
+  rc = make_tmap(&tmB, B, K, N, ldb, BK, BN);
+  if (rc) return rc;
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(g_attr_once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(w8a8_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return check_cuda(attr_err, "cudaFuncSetAttribute(w8a8_gemm_tc_kernel)");
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * ep.ksplits;
   const int grid = (int)std::min<int64_t>(tiles, sm_count());
   w8a8_gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tmA, tmB, ep);
-  return check_cuda(cudaGetLastError(), "w8a8_gemm_tc_kernel launch");
+  rc = check_cuda(cudaGetLastError(), "w8a8_gemm_tc_kernel launch");
+  if (rc || ep.ksplits == 1) return rc;
+  const int64_t total = M * N;
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)sm_count() * 8);
+  splitk_finalize_kernel<<<(unsigned)blocks, 256, 0, st>>>(ep);
+  return check_cuda(cudaGetLastError(), "splitk_finalize_kernel launch");
+}
+
+extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M, int64_t N,
+                            int64_t K, const void* sa, int sa_dtype, int sa_per_row, const void* sb, int sb_dtype,
+                            const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
+                            void* stream) {
+  return rb_w8a8_gemm_ws(A, lda, B, ldb, M, N, K, sa, sa_dtype, sa_per_row, sb, sb_dtype, bias, bias_dtype, out,
+                         ldo, out_dtype, nullptr, 0, stream);
 }

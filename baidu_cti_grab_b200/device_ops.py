@@ -298,12 +298,14 @@ def w8a8_gemm(a: torch.Tensor, b_nk: torch.Tensor, scale_a: Optional[torch.Tenso
         scale_b = scale_b.contiguous()
     if bias is not None:
         bias = bias.contiguous()
+    ws_elems = int(L.load().rb_w8a8_gemm_workspace_size(M, N, K))
+    ws = torch.empty((ws_elems,), dtype=torch.int32, device=dev) if ws_elems > 0 else None
     with torch.cuda.device(dev):
-        L.call("rb_w8a8_gemm", a.data_ptr(), a.stride(0), b_nk.data_ptr(), b_nk.stride(0), M, N, K,
+        L.call("rb_w8a8_gemm_ws", a.data_ptr(), a.stride(0), b_nk.data_ptr(), b_nk.stride(0), M, N, K,
                _ptr(scale_a), rb_dtype(scale_a) if scale_a is not None else 0, 1 if sa_per_row else 0,
                _ptr(scale_b), rb_dtype(scale_b) if scale_b is not None else 0, _ptr(bias),
                rb_dtype(bias) if bias is not None else 0, out.data_ptr(), out.stride(0), rb_dtype(out),
-               _stream(dev))
+               _ptr(ws), ws_elems, _stream(dev))
     return out
 
 

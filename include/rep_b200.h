@@ -163,6 +163,21 @@ int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int
                  int sb_dtype, const void* bias, int bias_dtype, void* out, int64_t ldo,
                  int out_dtype, void* stream);
 
+/*
+ * rb_w8a8_gemm with a caller-provided int32 workspace: for small M (fewer
+ * output tiles than SMs) the K dimension is split across CTAs, each split's
+ * int32 partial goes to the workspace, and a second kernel sums the splits in
+ * split order (exact) and applies the epilogue.  Same results as rb_w8a8_gemm,
+ * bit for bit.  rb_w8a8_gemm_workspace_size(M, N, K) gives the number of int32
+ * elements needed (0: no split for this shape); a smaller workspace runs unsplit.
+ * Replaces the same reference interfaces as rb_w8a8_gemm.
+ */
+int64_t rb_w8a8_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M, int64_t N,
+                    int64_t K, const void* sa, int sa_dtype, int sa_per_row, const void* sb, int sb_dtype,
+                    const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
+                    int32_t* workspace, int64_t workspace_elems, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -194,3 +194,29 @@ def test_watchdog_timeout_status(cuda_device):
     assert device_ops.device_error() == 0
     x = torch.ones(4, device=cuda_device)
     assert float(x.sum()) == 4.0
+
+
+@pytest.mark.parametrize("M", [1, 16, 256, 700])
+def test_gemm_split_k_equals_unsplit(cuda_device, M):
+    """The split-K path (workspace given) and the unsplit kernel (rb_w8a8_gemm) agree bit for bit."""
+    import torch
+    from baidu_cti_grab_b200 import _lib as L, device_ops
+
+    K, N = 14336, 512
+    assert L.load().rb_w8a8_gemm_workspace_size(M, N, K) > 0
+    gen = torch.Generator(device=cuda_device).manual_seed(M)
+    a = torch.randint(-128, 128, (M, K), dtype=torch.int8, device=cuda_device, generator=gen)
+    b = torch.randint(-128, 128, (N, K), dtype=torch.int8, device=cuda_device, generator=gen)
+    sa = torch.rand(M, device=cuda_device) * 1e-2
+    sb = torch.rand(N, device=cuda_device) * 1e-2
+    bias = torch.randn(N, device=cuda_device).to(torch.bfloat16)
+    split = device_ops.w8a8_gemm(a, b, sa, sb, torch.empty((M, N), dtype=torch.bfloat16, device=cuda_device),
+                                 bias=bias)
+    unsplit = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_device)
+    stream = torch.cuda.current_stream().cuda_stream
+    L.call("rb_w8a8_gemm", a.data_ptr(), K, b.data_ptr(), K, M, N, K, sa.data_ptr(), L.RB_F32, 1, sb.data_ptr(),
+           L.RB_F32, bias.data_ptr(), L.RB_BF16, unsplit.data_ptr(), N, L.RB_BF16, stream)
+    assert torch.equal(split, unsplit)
+    acc = device_ops.w8a8_gemm(a, b, None, None, torch.empty((M, N), dtype=torch.int32, device=cuda_device))
+    ref = a.double() @ b.double().t()
+    assert torch.equal(acc.double(), ref)
