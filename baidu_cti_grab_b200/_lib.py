@@ -45,6 +45,8 @@ SIGNATURES = {
     "rb_w8a8_gemm_ws": [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp, _i32, _vp,
                         _i64, _i32, _vp, _i64, _vp],
     "rb_w8a8_gemm_workspace_size": [_i64, _i64, _i64],
+    "rb_w8a8_gemm_noalloc": [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp, _i32, _vp,
+                             _i64, _i32, _vp],
     "rb_device_supported": [],
     "rb_device_error": [_i32],
     "rb_selftest_wait_timeout": [_u64, _vp],

@@ -838,3 +838,54 @@ extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64
   return rb_w8a8_gemm_ws(A, lda, B, ldb, M, N, K, sa, sa_dtype, sa_per_row, sb, sb_dtype, bias, bias_dtype, out,
                          ldo, out_dtype, nullptr, 0, stream);
 }
+
+// ----------------------------------------------------------------------------
+// Allocation-free entry point.  Some callers cannot allocate device memory on
+// their own: code that runs inside a CUDA-graph capture they do not control,
+// embedders whose memory is owned by another allocator (a framework pool, a
+// pre-sized arena in a latency-critical server), or plug-in hosts that forbid
+// cudaMalloc after start-up.  rb_w8a8_gemm_noalloc runs the same GEMM as
+// rb_w8a8_gemm_ws, taking its split-K workspace from the fixed device array
+// below instead of from the caller.
+//
+// * The array lives for the life of the process on every GPU that loads this
+//   library: kNoAllocScratchElems int32 = 20 MiB.  Any shape on a 148-SM B200
+//   fits (the split heuristic never asks for more than 148 * 128 * 256 int32);
+//   a shape that would need more is rejected with RB_ERR_VALUE.
+// * The first call on a device looks up the array's device address with
+//   cudaGetSymbolAddress (with that device current) and caches it; make that
+//   first call before any stream capture that includes this entry point.
+// * All calls share the one array.  Every partial a call reads was written
+//   earlier in the same call, so nothing needs clearing between calls, but
+//   two calls that run at the same time on the GPU (other streams, other host
+//   threads) overwrite each other's partials: serialise them.
+// * It calls no cudaMalloc, cudaFree or allocating library routine.
+static constexpr int64_t kNoAllocScratchElems = 5 * 1024 * 1024;
+static __device__ __align__(256) int32_t g_gemm_noalloc_scratch[kNoAllocScratchElems];
+static int32_t* g_noalloc_scratch_ptr[64];
+static cudaError_t g_noalloc_scratch_err[64];
+static std::once_flag g_noalloc_scratch_once[64];
+
+extern "C" int rb_w8a8_gemm_noalloc(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M,
+                                    int64_t N, int64_t K, const void* sa, int sa_dtype, int sa_per_row,
+                                    const void* sb, int sb_dtype, const void* bias, int bias_dtype, void* out,
+                                    int64_t ldo, int out_dtype, void* stream) {
+  const int64_t need = rb_w8a8_gemm_workspace_size(M, N, K);
+  if (need > kNoAllocScratchElems)
+    return fail(RB_ERR_VALUE,
+                "rb_w8a8_gemm_noalloc: M=%lld N=%lld K=%lld needs %lld int32 of split-K scratch, above the "
+                "library's fixed %lld; use rb_w8a8_gemm_ws with a workspace",
+                (long long)M, (long long)N, (long long)K, (long long)need, (long long)kNoAllocScratchElems);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return check_cuda(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(RB_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::call_once(g_noalloc_scratch_once[dev], [&] {
+    g_noalloc_scratch_err[dev] =
+        cudaGetSymbolAddress(reinterpret_cast<void**>(&g_noalloc_scratch_ptr[dev]), g_gemm_noalloc_scratch);
+  });
+  if (g_noalloc_scratch_err[dev] != cudaSuccess)
+    return check_cuda(g_noalloc_scratch_err[dev], "cudaGetSymbolAddress(g_gemm_noalloc_scratch)");
+  return rb_w8a8_gemm_ws(A, lda, B, ldb, M, N, K, sa, sa_dtype, sa_per_row, sb, sb_dtype, bias, bias_dtype, out,
+                         ldo, out_dtype, g_noalloc_scratch_ptr[dev], kNoAllocScratchElems, stream);
+}

@@ -178,6 +178,21 @@ int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, 
                     const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
                     int32_t* workspace, int64_t workspace_elems, void* stream);
 
+/*
+ * rb_w8a8_gemm_ws for callers that cannot allocate device memory themselves
+ * (inside a graph capture they do not own, under another allocator's pool, in
+ * hosts that forbid cudaMalloc after start-up).  No counterpart in the
+ * reference.  The split-K workspace comes from a fixed 20 MiB device array in
+ * the library (held on every GPU that loads it); shapes needing more are
+ * rejected with RB_ERR_VALUE.  The first call on a device resolves the array's
+ * address (make it before any stream capture).  Calls share the array, so
+ * calls that overlap on the GPU race; no state carries from one call to the
+ * next.  Same results as rb_w8a8_gemm, bit for bit; allocates nothing.
+ */
+int rb_w8a8_gemm_noalloc(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M, int64_t N,
+                         int64_t K, const void* sa, int sa_dtype, int sa_per_row, const void* sb, int sb_dtype,
+                         const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
