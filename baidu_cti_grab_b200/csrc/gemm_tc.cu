@@ -21,7 +21,11 @@
 //   warps 2-5   epilogue: tcgen05.ld 32x32b of the finished accumulator,
 //               dequant + bias in fp32, vector stores; releases the TMEM
 //               buffer so the MMA warp overlaps the next tile's main loop.
-// No thread-block clusters and no multicast loads are used.  Every mbarrier
+// For M >= RB_GEMM_PAIR_MIN_M a two-SM variant (namespace pair) runs each
+// 256x256 tile on a cluster of two CTAs with tcgen05.mma.cta_group::2; for
+// small M the one-SM kernel splits K across CTAs into an int32 workspace that
+// splitk_finalize_kernel sums in split order.  No TMA load carries a cluster
+// multicast (only tcgen05.commit signals both CTAs of a pair).  Every mbarrier
 // wait is bounded (common.cuh): on timeout the kernel records a watchdog code,
 // drains what it issued and returns instead of hanging.
 #include <cuda.h>
