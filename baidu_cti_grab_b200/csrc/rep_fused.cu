@@ -8,11 +8,12 @@
 // The concatenated [N, 14336] row never reaches HBM: one CTA owns one item,
 // warp w owns slots 4w..4w+3, and lane l of a warp owns columns 8l..8l+7 and
 // 256+8l..256+8l+7 of each of its slots (two 16-byte vectors of a bf16 row).
-// Those values stay in registers through the three LayerNorm passes and the
-// quantiser.  Statistics use the fixed ("canonical") reduction order stated in
-// the oracle: lane partials in column order, xor-butterfly 16..1 across the
-// warp, slot totals in slot order.  Every floating-point step is an explicit
-// round-to-nearest intrinsic so the result is reproducible bit for bit.
+// The pooled row sits in shared memory in the row dtype (28 KB for bf16)
+// between the statistics, the normalisation and the quantiser.  Statistics use
+// the fixed ("canonical") reduction order stated in the oracle: lane partials
+// in column order, xor-butterfly 16..1 across the warp per slot, then an
+// xor-butterfly over the slots.  Every floating-point step is an explicit
+// round-to-nearest operation so the result is reproducible bit for bit.
 //
 // HBM traffic per item (bf16 table, k ids per slot): 28*k*1 KB of table rows
 // + 28*k*8 B ids + 28*2*8 B offsets + 14336 B int8 + 4 B scale.
@@ -21,12 +22,6 @@
 namespace rb {
 
 constexpr int kSlotsPerWarp = 4;
-#ifndef RB_K1_SCALAR_LN
-#define RB_K1_SCALAR_LN 0  // 1: pass 2/3 in scalar fp32 instead of packed f32x2 (same results)
-#endif
-#ifndef RB_K1_PAIR_ASM
-#define RB_K1_PAIR_ASM 0  // 1: build the bf16-minus-mean pairs inside one asm block
-#endif
 #ifndef RB_K1_BF16_ROWS
 #define RB_K1_BF16_ROWS 2
 #endif
@@ -52,6 +47,7 @@ struct RepParams {
   const void* gamma;
   const void* beta;
   int ln_dtype;
+  int affine_v8;  // fp32 gamma/beta are 32-byte aligned: read with 256-bit loads
   float eps;
   int act_mode;
   const void* static_scale;
@@ -177,25 +173,6 @@ __device__ __forceinline__ float sub_hi(uint32_t w, float m) {  // bf16(hi) - m
   return d;
 }
 
-// (w's two bf16 - m) as an fp32 pair, built inside one asm block so that the
-// two halves can be allocated straight into the pair register
-__device__ __forceinline__ F2 sub_pair(uint32_t w, float m) {
-  F2 d;
-  asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 a, b;\n\tmov.b32 {lo, hi}, %1;\n\t"
-      "sub.rn.f32.bf16 a, lo, %2;\n\tsub.rn.f32.bf16 b, hi, %2;\n\tmov.b64 %0, {a, b};\n\t}"
-      : "=l"(d.r) : "r"(w), "f"(m));
-  return d;
-}
-// acc += (w - m)^2 for both halves of w (packed fma)
-__device__ __forceinline__ F2 sq_acc(F2 acc, uint32_t w, float m) {
-  F2 d;
-  asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 a, b;\n\t.reg .b64 t;\n\tmov.b32 {lo, hi}, %1;\n\t"
-      "sub.rn.f32.bf16 a, lo, %2;\n\tsub.rn.f32.bf16 b, hi, %2;\n\tmov.b64 t, {a, b};\n\t"
-      "fma.rn.f32x2 %0, t, t, %3;\n\t}"
-      : "=l"(d.r) : "r"(w), "f"(m), "l"(acc.r));
-  return d;
-}
-
 // ------------------------------------------------ row pieces per element type
 // A lane's 16 values of a 512-wide slot segment are columns 8l..8l+7 and
 // 256+8l..256+8l+7.  bf16 rows travel as 8 packed words (w[i] = elements
@@ -253,28 +230,61 @@ __device__ __forceinline__ void lds_pairs(const float* row, int s, int lane, F2*
   }
 }
 
-// 16 LayerNorm affine parameters of a lane's columns as fp32 pairs
-__device__ __forceinline__ void load_affine(const void* p, int dtype, int64_t col0, F2* out) {
-  if (dtype == RB_F32) {
-    const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + col0);
-    const float4 a = __ldg(q), b = __ldg(q + 1), c = __ldg(q + 64), d = __ldg(q + 65);
-    out[0] = f2(a.x, a.y); out[1] = f2(a.z, a.w); out[2] = f2(b.x, b.y); out[3] = f2(b.z, b.w);
-    out[4] = f2(c.x, c.y); out[5] = f2(c.z, c.w); out[6] = f2(d.x, d.y); out[7] = f2(d.z, d.w);
-    return;
+// 8 fp32 values of 32 contiguous bytes (one 256-bit load; p 32-byte aligned)
+__device__ __forceinline__ void ldg_v8(const float* p, float* v) {
+  asm("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+      : "l"(p));
+}
+
+// LayerNorm gamma and beta of one slot for one lane (its 16 columns), kept as
+// loaded.  The lane's columns 8l..8l+7 and 256+8l..256+8l+7 are read as two
+// contiguous pieces per tensor, so a warp reads each half-slot as one
+// contiguous block: 16 bytes per lane for 16-bit parameters, 32 bytes (one
+// 256-bit load, or two 128-bit loads when the tensors are only 16-byte
+// aligned) for fp32 parameters.
+template <typename TA>
+struct Affine;
+
+template <>
+struct Affine<uint16_t> {  // bf16 or fp16 parameters (p.ln_dtype says which)
+  uint32_t g[8], b[8];
+  __device__ __forceinline__ void load(const RepParams& p, int s, int lane) {
+    ldg_words(reinterpret_cast<const uint16_t*>(p.gamma) + s * kDim, lane, g);
+    ldg_words(reinterpret_cast<const uint16_t*>(p.beta) + s * kDim, lane, b);
   }
-  const uint4* q = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + col0);
-  const uint4 a = __ldg(q), c = __ldg(q + 32);
-  const uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (dtype == RB_BF16) {
-      out[i] = bf2(w[i]);
+  static __device__ __forceinline__ F2 widen(uint32_t w, bool bf) {
+    if (bf) return bf2(w);
+    const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    return f2(h.x, h.y);
+  }
+  __device__ __forceinline__ F2 gamma(int i, bool bf) const { return widen(g[i], bf); }
+  __device__ __forceinline__ F2 beta(int i, bool bf) const { return widen(b[i], bf); }
+};
+
+template <>
+struct Affine<float> {
+  float g[16], b[16];
+  __device__ __forceinline__ void load(const RepParams& p, int s, int lane) {
+    const float* gp = reinterpret_cast<const float*>(p.gamma) + s * kDim + 8 * lane;
+    const float* bp = reinterpret_cast<const float*>(p.beta) + s * kDim + 8 * lane;
+    if (p.affine_v8) {
+      ldg_v8(gp, g);
+      ldg_v8(gp + 256, g + 8);
+      ldg_v8(bp, b);
+      ldg_v8(bp + 256, b + 8);
     } else {
-      const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-      out[i] = f2(h.x, h.y);
+      ld4(gp, g); ld4(gp + 4, g + 4); ld4(gp + 256, g + 8); ld4(gp + 260, g + 12);
+      ld4(bp, b); ld4(bp + 4, b + 4); ld4(bp + 256, b + 8); ld4(bp + 260, b + 12);
     }
   }
-}
+  static __device__ __forceinline__ void ld4(const float* p, float* v) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  }
+  __device__ __forceinline__ F2 gamma(int i, bool) const { return f2(g[2 * i], g[2 * i + 1]); }
+  __device__ __forceinline__ F2 beta(int i, bool) const { return f2(b[2 * i], b[2 * i + 1]); }
+};
 
 // Ask the copy engine to bring `bytes` at `p` into L2 (no registers, no wait).
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
@@ -293,24 +303,30 @@ __device__ __forceinline__ V sel4(const V* a, int j) {
   return j == 0 ? a[0] : (j == 1 ? a[1] : (j == 2 ? a[2] : a[3]));
 }
 
-// One CTA per item.  Warp w owns slots 4w..4w+3.  Per slot it sums the bag's
-// table rows in bag order (kRows loads in flight; every row of the warp's id
-// window was already requested into L2 by a bulk prefetch), rounds the sum to
-// the row dtype into the shared-memory row and adds the slot's first-pass
-// LayerNorm partial (canonical order: even / odd accumulators per lane,
-// butterfly, slot order).  Then: variance pass, normalise + affine (y rounded
-// to the row dtype, written back in place) with the absmax, and the int8
-// quantiser.  bf16 rows stay packed in shared memory (28 KB per item) and
-// enter fp32 arithmetic through the mixed-precision add/sub.
-template <typename T, int MODE, bool kFull4>
-__global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant__ RepParams p) {
+// One CTA per item.  Warp w owns slots 4w..4w+3 and lane l owns 16 columns
+// of each (file header).  Per slot the warp sums the bag's table rows in bag
+// order (kRows rows in flight; the rows of the warp's id window were already
+// requested into L2 by bulk prefetches), rounds the sums to the row dtype into
+// the item's shared-memory row and, from the rounded values still in
+// registers, takes the slot sum T_s (lane partials, xor butterfly) and the
+// lane partials of Q_s = sum (x - T_s/512)^2.  After one barrier every warp
+// combines the slot statistics into mean and rstd itself, normalises its
+// slots in place (y rounded to the row dtype) with the absmax, and after a
+// second barrier quantises them to int8.  bf16 rows stay packed in shared
+// memory (28 KB per item) and enter fp32 arithmetic through the
+// mixed-precision add/sub.  TA is the storage type of gamma/beta (uint16_t
+// for bf16/fp16, float).  With bf16 rows the register budget (48 per
+// thread) keeps five 7-warp CTAs resident per SM: the gather's latency needs
+// that occupancy more than the code needs registers.  An fp32 row takes 56 KB
+// of shared memory, so at most three CTAs fit and the budget is larger.
+template <typename T, int MODE, bool kFull4, typename TA>
+__global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(const __grid_constant__ RepParams p) {
   constexpr bool kBf16 = sizeof(T) == 2;
   constexpr int kRows = kBf16 ? RB_K1_BF16_ROWS : 2;  // table rows a warp holds in registers
   extern __shared__ __align__(16) uint8_t s_raw[];
   __shared__ float s_tot[RB_MAX_SLOTS];  // per-slot sums T_s
   __shared__ float s_q[RB_MAX_SLOTS];    // per-slot centred square sums Q_s
   __shared__ float s_wmax[8];
-  __shared__ float s_stat[2];  // mean, rstd
   uint32_t* s_words = reinterpret_cast<uint32_t*>(s_raw);  // bf16 row: 256 words per slot
   float* s_f32 = reinterpret_cast<float*>(s_raw);          // fp32 row: 512 floats per slot
 
@@ -323,12 +339,23 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
   // RepEncoder), so the per-slot loops unroll with constant offsets
   const int nsl = kFull4 ? kSlotsPerWarp : max(0, min(kSlotsPerWarp, S - slot0));
 
-  // pooled slot s of this warp is final in `acc` (fp32, not yet rounded):
-  // round to T, keep it in shared memory, return the lane's first-pass partial
-  auto finish_slot = [&](int s, float* acc) -> float {
+  // lane partials of Q_s of the warp's slots (0 for slots past S)
+  float part[kSlotsPerWarp] = {0.0f, 0.0f, 0.0f, 0.0f};
+  auto put_part = [&](int j, float v) {
+#pragma unroll
+    for (int jj = 0; jj < kSlotsPerWarp; ++jj)
+      if (jj == j) part[jj] = v;
+  };
+
+  // the warp's j-th slot is pooled in `acc` (fp32, not yet rounded): round it
+  // to T into shared memory (and the optional pooled output), then take the
+  // slot statistics from the rounded values
+  auto finish_slot = [&](int j, const float* acc) {
+    const int s = slot0 + j;
     float a0 = 0.0f, a1 = 0.0f;
+    uint32_t w[8];
+    F2 x[8];
     if constexpr (kBf16) {
-      uint32_t w[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
       st_words(s_words + s * 256, lane, w);
@@ -337,13 +364,14 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
       } else if (p.pooled != nullptr) {
         st_words(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, w);
       }
+      if constexpr (MODE != kGatherPool) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        a0 = add_lo(a0, w[i]);
-        a1 = add_hi(a1, w[i]);
+        for (int i = 0; i < 8; ++i) {
+          a0 = add_lo(a0, w[i]);
+          a1 = add_hi(a1, w[i]);
+        }
       }
     } else {
-      F2 x[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) x[i] = f2(acc[2 * i], acc[2 * i + 1]);
       sts_pairs(s_f32, s, lane, x);
@@ -352,27 +380,44 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
       } else if (p.pooled != nullptr) {
         stg_pairs(reinterpret_cast<float*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, x);
       }
+      if constexpr (MODE != kGatherPool) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        a0 = __fadd_rn(a0, acc[2 * i]);
-        a1 = __fadd_rn(a1, acc[2 * i + 1]);
+        for (int i = 0; i < 8; ++i) {
+          a0 = __fadd_rn(a0, acc[2 * i]);
+          a1 = __fadd_rn(a1, acc[2 * i + 1]);
+        }
       }
     }
-    return __fadd_rn(a0, a1);
-  };
-  // lane partials of the warp's slots (0 for slots past S), reduced together
-  float part[kSlotsPerWarp] = {0.0f, 0.0f, 0.0f, 0.0f};
-  auto put_part = [&](int j, float v) {
+    if constexpr (MODE != kGatherPool) {
+      float tot = __fadd_rn(a0, a1);
 #pragma unroll
-    for (int jj = 0; jj < kSlotsPerWarp; ++jj)
-      if (jj == j) part[jj] = v;
+      for (int d = 16; d >= 1; d >>= 1) tot = __fadd_rn(tot, __shfl_xor_sync(0xffffffffu, tot, d));
+      const float m = __fmul_rn(tot, 0.001953125f);  // T_s / 512, exact
+      F2 q = f2(0.0f, 0.0f);
+      if constexpr (kBf16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const F2 d = f2(sub_lo(w[i], m), sub_hi(w[i], m));
+          q = fma2(d, d, q);
+        }
+      } else {
+        const F2 m2 = f2(m, m);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const F2 d = sub2(x[i], m2);
+          q = fma2(d, d, q);
+        }
+      }
+      const float2 qv = un(q);
+      put_part(j, __fadd_rn(qv.x, qv.y));
+      if (lane == 0) s_tot[s] = tot;
+    }
   };
 
   if constexpr (MODE == kDenseLnQuant) {
 #pragma unroll
     for (int j = 0; j < nsl; ++j) {
-      const int s = slot0 + j;
-      const T* xseg = reinterpret_cast<const T*>(p.xs[s]) + item * p.ldx;
+      const T* xseg = reinterpret_cast<const T*>(p.xs[slot0 + j]) + item * p.ldx;
       float acc[16];
       if constexpr (kBf16) {
         uint32_t w[8];
@@ -392,7 +437,7 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
           acc[2 * i + 1] = v.y;
         }
       }
-      put_part(j, finish_slot(s, acc));
+      finish_slot(j, acc);
     }
   } else {
     // ---- bag bounds of this warp's slots: lanes 0-3 starts, lanes 4-7 ends
@@ -487,99 +532,55 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
           }
         }
       }
-      put_part(j, finish_slot(slot0 + j, acc));
+      finish_slot(j, acc);
     }
   }
 
   if constexpr (MODE != kGatherPool) {
     const float H = (float)(S * kDim);
-    // ---- per-slot statistics: T_s (sum), then Q_s = sum (x - T_s/512)^2
-    const float slot_sum = warp_sum4_butterfly(part[0], part[1], part[2], part[3], lane);  // lanes 8j..: slot j
-    float m_slot[kSlotsPerWarp];
-#pragma unroll
-    for (int j = 0; j < kSlotsPerWarp; ++j)
-      m_slot[j] = __fmul_rn(__shfl_sync(0xffffffffu, slot_sum, 8 * j), 0.001953125f);  // T_j / 512, exact
-#pragma unroll
-    for (int j = 0; j < kSlotsPerWarp; ++j) {
-      float q = 0.0f;
-      if (j < nsl) {
-        const int s = slot0 + j;
-        F2 a = f2(0.0f, 0.0f);
-        if constexpr (kBf16) {
-          uint32_t w[8];
-          ld_words(s_words + s * 256, lane, w);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const F2 d = f2(sub_lo(w[i], m_slot[j]), sub_hi(w[i], m_slot[j]));
-            a = fma2(d, d, a);
-          }
-        } else {
-          F2 x[8];
-          lds_pairs(s_f32, s, lane, x);
-          const F2 m2 = f2(m_slot[j], m_slot[j]);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const F2 d = sub2(x[i], m2);
-            a = fma2(d, d, a);
-          }
-        }
-        const float2 v = un(a);
-        q = __fadd_rn(v.x, v.y);
-      }
-      part[j] = q;
-    }
-    const float slot_q = warp_sum4_butterfly(part[0], part[1], part[2], part[3], lane);
+    const bool bf_affine = p.ln_dtype == RB_BF16;
+    const float slot_q = warp_sum4_butterfly(part[0], part[1], part[2], part[3], lane);  // lanes 8j..: slot j
     {
       const int j = lane >> 3;
-      if ((lane & 7) == 0 && j < nsl) {
-        s_tot[slot0 + j] = slot_sum;
-        s_q[slot0 + j] = slot_q;
-      }
+      if ((lane & 7) == 0 && j < nsl) s_q[slot0 + j] = slot_q;
     }
+    // the first slot's gamma/beta are requested before the barrier
+    Affine<TA> aff;
+    if (nsl > 0) aff.load(p, slot0, lane);
     __syncthreads();
-    if (threadIdx.x == 0) {
-      // combine the slots in slot order (Chan's parallel variance update)
-      float t = 0.0f;
-      for (int s = 0; s < S; ++s) t = __fadd_rn(t, s_tot[s]);
-      const float mean = __fdiv_rn(t, H);
-      float m2 = 0.0f;
-      for (int s = 0; s < S; ++s) {
-        const float d = __fsub_rn(__fmul_rn(s_tot[s], 0.001953125f), mean);
-        m2 = __fadd_rn(m2, __fadd_rn(s_q[s], __fmul_rn(512.0f, __fmul_rn(d, d))));
-      }
-      const float var = __fdiv_rn(m2, H);
-      s_stat[0] = mean;
-      s_stat[1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
+    // every warp combines the slots itself (lane s holds slot s; lanes past S
+    // contribute zero): xor-butterfly of the slot sums -> mean, then of
+    // Q_s + 512 (m_s - mean)^2 (Chan's parallel update) -> M2
+    float mean, rstd;
+    {
+      const float t_l = lane < S ? s_tot[lane] : 0.0f;
+      const float q_l = lane < S ? s_q[lane] : 0.0f;
+      float t = t_l;
+#pragma unroll
+      for (int d = 16; d >= 1; d >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, d));
+      mean = __fdiv_rn(t, H);
+      const float dm = __fsub_rn(__fmul_rn(t_l, 0.001953125f), mean);
+      float c = lane < S ? __fadd_rn(q_l, __fmul_rn(512.0f, __fmul_rn(dm, dm))) : 0.0f;
+#pragma unroll
+      for (int d = 16; d >= 1; d >>= 1) c = __fadd_rn(c, __shfl_xor_sync(0xffffffffu, c, d));
+      const float var = __fdiv_rn(c, H);
+      rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
     }
-    __syncthreads();
-    const float mean = s_stat[0];
     const F2 mean2 = f2(mean, mean);
-    const float rstd = s_stat[1];
     const F2 rstd2 = f2(rstd, rstd);
-    // ---- pass 3: y = fma(rstd * (x - mean), gamma, beta) rounded to T, in place; absmax
+    // ---- y = fma(rstd * (x - mean), gamma, beta) rounded to T, in place; absmax
     float amax = 0.0f;
 #pragma unroll
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
-      F2 g[8], b[8], y[8];
-      const int64_t col0 = (int64_t)s * kDim + 8 * lane;
-      load_affine(p.gamma, p.ln_dtype, col0, g);
-      load_affine(p.beta, p.ln_dtype, col0, b);
+      if (j > 0) aff.load(p, s, lane);
       if constexpr (kBf16) {
         uint32_t w[8];
         ld_words(s_words + s * 256, lane, w);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-#if RB_K1_SCALAR_LN
-          const float2 gg = un(g[i]), bb = un(b[i]);
-          const float2 v = make_float2(__fmaf_rn(__fmul_rn(rstd, sub_lo(w[i], mean)), gg.x, bb.x),
-                                       __fmaf_rn(__fmul_rn(rstd, sub_hi(w[i], mean)), gg.y, bb.y));
-#elif RB_K1_PAIR_ASM
-          const float2 v = un(fma2(mul2(rstd2, sub_pair(w[i], mean)), g[i], b[i]));
-#else
           const F2 d = f2(sub_lo(w[i], mean), sub_hi(w[i], mean));
-          const float2 v = un(fma2(mul2(rstd2, d), g[i], b[i]));
-#endif
+          const float2 v = un(fma2(mul2(rstd2, d), aff.gamma(i, bf_affine), aff.beta(i, bf_affine)));
           // rounding to bf16 is monotonic and symmetric, so the absmax of the
           // rounded row is the rounded absmax of the fp32 row
           amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
@@ -588,10 +589,11 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
         st_words(s_words + s * 256, lane, w);
         if (p.ln != nullptr) st_words(reinterpret_cast<T*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, w);
       } else {
-        F2 x[8];
+        F2 x[8], y[8];
         lds_pairs(s_f32, s, lane, x);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = fma2(mul2(rstd2, sub2(x[i], mean2)), g[i], b[i]);
+        for (int i = 0; i < 8; ++i)
+          y[i] = fma2(mul2(rstd2, sub2(x[i], mean2)), aff.gamma(i, bf_affine), aff.beta(i, bf_affine));
         sts_pairs(s_f32, s, lane, y);
         if (p.ln != nullptr) stg_pairs(reinterpret_cast<float*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, y);
 #pragma unroll
@@ -606,7 +608,7 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
     amax = warp_max(amax);
     if (lane == 0) s_wmax[warp] = amax;
     __syncthreads();
-    // every thread derives the quantiser scale (no second barrier)
+    // every thread derives the quantiser scale (no further barrier)
     float inv;
     if (p.act_mode == RB_ACT_DYNAMIC) {
       float m = 0.0f;
@@ -619,7 +621,7 @@ __global__ void __launch_bounds__(256, 4) rep_fused_kernel(const __grid_constant
     }
     const F2 inv2 = f2(inv, inv);
     const bool clamp = p.act_mode == RB_ACT_STATIC;
-    // ---- pass 4: int8 = clamp(round_half_away(y * inv), -128, 127)
+    // ---- int8 = clamp(round_half_away(y * inv), -128, 127)
 #pragma unroll
     for (int j = 0; j < nsl; ++j) {
       const int s = slot0 + j;
@@ -687,9 +689,16 @@ static int launch_rep(const RepParams& p, int row_dtype, cudaStream_t stream) {
   const size_t smem = (size_t)p.num_slots * kDim * dtype_size(row_dtype);
   cudaError_t e = cudaSuccess;
   const bool full4 = p.num_slots % kSlotsPerWarp == 0;
+  // gamma/beta storage: 16-bit words or fp32 (the pooling-only mode reads neither)
+  const bool a16 = MODE != kGatherPool && p.ln_dtype != RB_F32;
   auto kern = row_dtype == RB_BF16
-                  ? (full4 ? rep_fused_kernel<__nv_bfloat16, MODE, true> : rep_fused_kernel<__nv_bfloat16, MODE, false>)
-                  : (full4 ? rep_fused_kernel<float, MODE, true> : rep_fused_kernel<float, MODE, false>);
+                  ? (full4 ? (a16 ? rep_fused_kernel<__nv_bfloat16, MODE, true, uint16_t>
+                                  : rep_fused_kernel<__nv_bfloat16, MODE, true, float>)
+                           : (a16 ? rep_fused_kernel<__nv_bfloat16, MODE, false, uint16_t>
+                                  : rep_fused_kernel<__nv_bfloat16, MODE, false, float>))
+                  : (full4 ? (a16 ? rep_fused_kernel<float, MODE, true, uint16_t> : rep_fused_kernel<float, MODE, true, float>)
+                           : (a16 ? rep_fused_kernel<float, MODE, false, uint16_t>
+                                  : rep_fused_kernel<float, MODE, false, float>));
   if (smem > 48 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess) kern<<<grid, block, smem, stream>>>(p);
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(rep_fused_kernel)");
@@ -757,6 +766,7 @@ extern "C" int rb_rep_gather_ln_quant(const void* table, int table_dtype, int64_
   p.num_items = num_items;
   p.gamma = ln_gamma;
   p.beta = ln_beta;
+  p.affine_v8 = aligned(ln_gamma, 32) && aligned(ln_beta, 32);
   p.ln_dtype = ln_dtype;
   p.eps = eps;
   p.act_mode = act_mode;
@@ -815,6 +825,7 @@ static int layernorm_quant_common(RepParams& p, int x_dtype, int64_t num_items, 
   p.num_items = num_items;
   p.gamma = ln_gamma;
   p.beta = ln_beta;
+  p.affine_v8 = aligned(ln_gamma, 32) && aligned(ln_beta, 32);
   p.ln_dtype = ln_dtype;
   p.eps = eps;
   p.act_mode = act_mode;

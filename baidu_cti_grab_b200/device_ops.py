@@ -81,10 +81,11 @@ def cached_derived(src: torch.Tensor, tag: str, make):
     return value
 
 
-def _affine_f32(t: torch.Tensor) -> torch.Tensor:
-    """fp32 copy of a LayerNorm parameter (exact widening); the kernel then
-    reads 4 values per load instead of unpacking 16-bit values."""
-    if t.dtype == torch.float32:
+def _affine_param(t: torch.Tensor) -> torch.Tensor:
+    """A LayerNorm parameter as the kernels read it: bf16, fp16 or fp32,
+    contiguous (other dtypes are widened to fp32 once and cached).  16-bit
+    parameters are read as they are: half the bytes of an fp32 copy."""
+    if t.dtype in (torch.bfloat16, torch.float16, torch.float32):
         return t.contiguous()
     return cached_derived(t, "affine_f32", lambda x: x.detach().float().contiguous())
 
@@ -120,8 +121,8 @@ def rep_gather_ln_quant(table: torch.Tensor, slot_values: Sequence[torch.Tensor]
             scale = torch.empty((n_items,), dtype=torch.float32, device=dev) if scale_out is None else scale_out
     pooled = torch.empty((n_items, H), dtype=table.dtype, device=dev) if want_pooled else None
     ln = torch.empty((n_items, H), dtype=table.dtype, device=dev) if (want_ln or mode == L.RB_ACT_NONE) else None
-    gamma = _affine_f32(gamma)
-    beta = _affine_f32(beta)
+    gamma = _affine_param(gamma)
+    beta = _affine_param(beta)
     if static_scale is not None:
         static_scale = static_scale.contiguous()
     with torch.cuda.device(dev):
@@ -169,8 +170,8 @@ def layernorm_quant(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, ep
     q = torch.empty((n, H), dtype=torch.int8, device=dev) if mode != L.RB_ACT_NONE else None
     scale = torch.empty((n,), dtype=torch.float32, device=dev) if mode == L.RB_ACT_DYNAMIC else None
     ln = torch.empty((n, H), dtype=x.dtype, device=dev) if (want_ln or mode == L.RB_ACT_NONE) else None
-    gamma = _affine_f32(gamma)
-    beta = _affine_f32(beta)
+    gamma = _affine_param(gamma)
+    beta = _affine_param(beta)
     if static_scale is not None:
         static_scale = static_scale.contiguous()
     with torch.cuda.device(dev):
@@ -197,8 +198,8 @@ def layernorm_quant_slots(slot_rows: Sequence[torch.Tensor], gamma: torch.Tensor
     q = torch.empty((n, H), dtype=torch.int8, device=dev) if mode != L.RB_ACT_NONE else None
     scale = torch.empty((n,), dtype=torch.float32, device=dev) if mode == L.RB_ACT_DYNAMIC else None
     ln = torch.empty((n, H), dtype=slot_rows[0].dtype, device=dev) if (want_ln or mode == L.RB_ACT_NONE) else None
-    gamma = _affine_f32(gamma)
-    beta = _affine_f32(beta)
+    gamma = _affine_param(gamma)
+    beta = _affine_param(beta)
     if static_scale is not None:
         static_scale = static_scale.contiguous()
     with torch.cuda.device(dev):

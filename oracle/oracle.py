@@ -22,6 +22,7 @@ LIB_PATH = os.path.join(HERE, "librep_oracle.so")
 
 F32, BF16, F16, I32 = 0, 1, 2, 3
 _DT = {"float32": F32, "bfloat16": BF16, "float16": F16}
+MAX_SLOTS = 32  # the canonical LayerNorm combines the slots by a 32-wide butterfly
 
 _lib = None
 
@@ -113,7 +114,8 @@ def layernorm_rows(x: np.ndarray, gamma: np.ndarray, beta: np.ndarray, eps: floa
     gamma = np.ascontiguousarray(gamma, dtype=np.float32)
     beta = np.ascontiguousarray(beta, dtype=np.float32)
     m, h = x.shape
-    assert h % 512 == 0
+    if h % 512 != 0 or not 1 <= h // 512 <= MAX_SLOTS:
+        raise ValueError(f"row width {h} is not 512 x [1, {MAX_SLOTS}] slots")
     y = np.empty_like(x)
     mean = np.empty(m, dtype=np.float32)
     rstd = np.empty(m, dtype=np.float32)
@@ -202,6 +204,8 @@ def rep_forward(table: np.ndarray, table_dtype: str, batch: Dict[object, object]
     pooled and LayerNorm rows (fp32 values of the row dtype)."""
     if num_slots is None:
         num_slots = max(k for k in batch if isinstance(k, int))
+    if not 1 <= num_slots <= MAX_SLOTS:
+        raise ValueError(f"num_slots must be in [1, {MAX_SLOTS}], got {num_slots}")
     table = np.ascontiguousarray(table)
     vals = [np.ascontiguousarray(batch[s][0], dtype=np.int64) for s in range(1, num_slots + 1)]
     offs = [np.ascontiguousarray(batch[s][1], dtype=np.int64) for s in range(1, num_slots + 1)]

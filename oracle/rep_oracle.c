@@ -35,13 +35,13 @@
  * them in that order, elements at even positions accumulate into a0 and odd
  * positions into a1 (both from 0.0f), and the lane partial is a0 + a1; the
  * 32 lane partials are combined by an xor-butterfly with distances 16, 8, 4,
- * 2, 1 (p[l] = p[l] + p[l^d]); the slot totals are then added in slot order
- * starting from 0.0f.  (The even/odd split is what a packed two-wide fp32
- * add computes.)  Per slot s this order gives the sum T_s of x and, with the
- * slot mean m_s = T_s / 512, the centred square sum Q_s of (x - m_s)^2
- * (fmaf(d, d, acc) per element).  The slots are then combined in slot order:
- *   mean = (sum_s T_s) / H
- *   M2   = sum_s (Q_s + 512 * (m_s - mean)^2)       (Chan's parallel update)
+ * 2, 1 (p[l] = p[l] + p[l^d]).  (The even/odd split is what a packed two-wide
+ * fp32 add computes.)  Per slot s this order gives the sum T_s of x and, with
+ * the slot mean m_s = T_s / 512, the centred square sum Q_s of (x - m_s)^2
+ * (fmaf(d, d, acc) per element).  The slots are then combined by the same
+ * 32-wide xor-butterfly, slot s in position s and 0.0f in positions S..31:
+ *   mean = butterfly_s(T_s) / H
+ *   M2   = butterfly_s(Q_s + 512 * (m_s - mean)^2)   (Chan's parallel update)
  *   var  = M2 / H;  rstd = 1.0f / sqrtf(var + eps)
  *   y    = fmaf(rstd * (x - mean), gamma, beta)   (then RNE to the row dtype)
  * Division and square root are IEEE correctly rounded here and in the kernel.
@@ -177,6 +177,16 @@ void rbo_embedding_bag_sum(const void* table, int table_dtype, int64_t num_rows,
 }
 
 /* --------------------------------------------------- canonical LayerNorm */
+/* p[0] after the xor-butterfly p[l] = p[l] + p[l^d], d = 16, 8, 4, 2, 1 */
+static float butterfly32(float* p) {
+    for (int dist = 16; dist >= 1; dist >>= 1) {
+        float q[32];
+        for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ dist];
+        memcpy(p, q, 32 * sizeof(float));
+    }
+    return p[0];
+}
+
 static float canonical_slot_sum(const float* seg, float mean, int centred) {
     float p[32];
     for (int l = 0; l < 32; ++l) {
@@ -194,38 +204,36 @@ static float canonical_slot_sum(const float* seg, float mean, int centred) {
         }
         p[l] = a[0] + a[1];
     }
-    for (int dist = 16; dist >= 1; dist >>= 1) {
-        float q[32];
-        for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ dist];
-        memcpy(p, q, sizeof(p));
-    }
-    return p[0];
+    return butterfly32(p);
 }
 
 /*
  * LayerNorm of one row x[S*512] (values already in the row dtype, widened to
  * fp32).  gamma/beta widened to fp32.  y receives fp32 values rounded to
  * out_dtype (so y[] holds exactly what the kernel stores).  mean/rstd out.
+ * 1 <= n_slots <= 32 (the slots are combined by a 32-wide butterfly).
  */
 void rbo_layernorm_row(const float* x, int64_t n_slots, const float* gamma, const float* beta,
                        float eps, int out_dtype, float* y, float* mean_out, float* rstd_out) {
     const int64_t H = n_slots * 512;
-    float t1 = 0.0f;
-    float slot_sum[64], slot_q[64];
+    float slot_sum[32], slot_q[32], p[32];
+    for (int64_t s = 0; s < 32; ++s) {
+        slot_sum[s] = 0.0f;
+        slot_q[s] = 0.0f;
+    }
     for (int64_t s = 0; s < n_slots; ++s) {
         slot_sum[s] = canonical_slot_sum(x + s * 512, 0.0f, 0);
         const float m_s = slot_sum[s] / 512.0f;
         slot_q[s] = canonical_slot_sum(x + s * 512, m_s, 1);
-        t1 = t1 + slot_sum[s];
     }
-    const float mean = t1 / (float)H;
-    /* Chan's combination of the per-slot centred sums, in slot order */
-    float m2 = 0.0f;
-    for (int64_t s = 0; s < n_slots; ++s) {
+    memcpy(p, slot_sum, sizeof(p));
+    const float mean = butterfly32(p) / (float)H;
+    /* Chan's combination of the per-slot centred sums, butterfly over slots */
+    for (int64_t s = 0; s < 32; ++s) {
         const float d = slot_sum[s] / 512.0f - mean;
-        m2 = m2 + (slot_q[s] + 512.0f * (d * d));
+        p[s] = s < n_slots ? slot_q[s] + 512.0f * (d * d) : 0.0f;
     }
-    const float var = m2 / (float)H;
+    const float var = butterfly32(p) / (float)H;
     const float rstd = 1.0f / sqrtf(var + eps);
     for (int64_t k = 0; k < H; ++k) {
         float d = x[k] - mean;

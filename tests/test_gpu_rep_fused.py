@@ -109,8 +109,10 @@ def test_k1_synthetic_bit_exact(cuda_device, dt, seed, users):
     assert np.array_equal(scale.cpu().numpy(), oscale)
 
 
-def test_k1_fp32_affine_params_on_bf16_rows(cuda_device):
-    """LayerNorm gamma/beta kept in fp32 while the table is bf16 (mixed module dtypes)."""
+@pytest.mark.parametrize("param_dtype,offset", [("float32", 0), ("float32", 4), ("float16", 0), ("bfloat16", 8)])
+def test_k1_affine_param_dtypes_on_bf16_rows(cuda_device, param_dtype, offset):
+    """LayerNorm gamma/beta in fp32 (32-byte aligned, and only 16-byte aligned:
+    a view 4 floats into a buffer), fp16 or bf16 while the table is bf16."""
     import torch
     from oracle import oracle as O
 
@@ -120,8 +122,18 @@ def test_k1_fp32_affine_params_on_bf16_rows(cuda_device):
     rng = np.random.default_rng(5)
     g32 = (1.0 + 0.3 * rng.standard_normal(28 * 512)).astype(np.float32)
     b32 = (0.1 * rng.standard_normal(28 * 512)).astype(np.float32)
-    q, scale, _, ln = _run_k1(torch, table, vals, offs, torch.from_numpy(g32).to(cuda_device),
-                              torch.from_numpy(b32).to(cuda_device), eps)
+    tdt = getattr(torch, param_dtype)
+
+    def put(a):
+        buf = torch.zeros(a.size + offset, dtype=tdt, device=cuda_device)
+        view = buf[offset:]
+        view.copy_(torch.from_numpy(a))
+        return view
+
+    g, b = put(g32), put(b32)
+    assert g.data_ptr() % 16 == 0
+    g32, b32 = g.float().cpu().numpy(), b.float().cpu().numpy()  # the values the kernel sees
+    q, scale, _, ln = _run_k1(torch, table, vals, offs, g, b, eps)
     oq, oscale, _, oln = O.rep_forward(table_np, dt, batch, g32, b32, eps, intermediates=True)
     assert np.array_equal(_row_f32(torch, ln), oln)
     assert np.array_equal(q.cpu().numpy(), oq)
