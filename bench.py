@@ -57,6 +57,8 @@ def parse_args(argv=None):
     ap.add_argument("--rows-per-slot", type=int, default=None,
                     help="override table rows per slot (smaller cases for profiling captures)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunk-items", type=int, default=None,
+                    help="items per pipeline chunk on the e2e path (default: the pipeline's; 0: whole batches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-items", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -359,9 +361,10 @@ def b200_arm(args):
     # batches, H2D / forward / D2H of successive batches overlapped on streams
     e2e = None
     if not args.no_e2e:
-        from baidu_cti_grab_b200.pipeline import HostPipeline, pack_batch
+        from baidu_cti_grab_b200.pipeline import DEFAULT_CHUNK_ITEMS, HostPipeline, pack_batch
 
-        packed = [pack_batch(b) for b in host_batches]
+        chunk_items = DEFAULT_CHUNK_ITEMS if args.e2e_chunk_items is None else (args.e2e_chunk_items or None)
+        packed = [pack_batch(b, chunk_items=chunk_items) for b in host_batches]
         max_ids = max(st[1] for st in stats)
         pipe = HostPipeline(rep, max_ids=max_ids, max_items=n_items_max)
         host_outs = [torch.empty((st[0], D_OUT), dtype=bf).pin_memory() for st in stats]
@@ -379,7 +382,8 @@ def b200_arm(args):
         torch.cuda.synchronize()
         e_ms = e0.elapsed_time(e1)
         e_items = sum(pb.num_items for pb in seq)
-        e2e = [e_items, e_ms, sum(pb.nbytes for pb in seq) / K, sum(pb.num_items * D_OUT * 2 for pb in seq) / K]
+        e2e = [e_items, e_ms, sum(pb.nbytes for pb in seq) / K, sum(pb.num_items * D_OUT * 2 for pb in seq) / K,
+               chunk_items]
 
     # ---- max over ranks
     vals = torch.tensor([ms, e2e[1] if e2e else 0.0, k1_ms, k2_ms], dtype=torch.float64, device=dev)
@@ -443,9 +447,10 @@ def b200_arm(args):
         if e2e is not None:
             line["e2e"] = {"value": round(e2e_items_all / (e2e_ms_max * 1e-3), 1), "unit": "items/s",
                            "h2d_bytes_per_step": int(e2e[2]), "d2h_bytes_per_step": int(e2e[3]),
-                           "api": "HostPipeline.run -> rep_encoder_forward (fuse_mode b200): one pinned H2D copy of "
-                                  "the packed ids/offsets and one D2H copy of the bf16 output per batch, "
-                                  "overlapped across successive batches"}
+                           "chunk_items": e2e[4],
+                           "api": "HostPipeline.run -> rep_encoder_forward (fuse_mode b200): per chunk of a batch's "
+                                  "items one pinned H2D copy of its packed ids/offsets, K1 + K2, and one D2H copy "
+                                  "of its bf16 output rows; copies of one chunk overlap the kernels of the next"}
 
     # ---- CPU baseline (rank 0, N=1 only)
     if world > 1:

@@ -173,8 +173,10 @@ def test_static_quantised_checkpoint_layer(cuda_device):
     assert torch.equal(out, ref)
 
 
-def test_host_pipeline_matches_direct_forward(cuda_device):
-    """HostPipeline (overlapped H2D / forward / D2H) returns exactly the direct forward's output."""
+@pytest.mark.parametrize("chunk_items", [None, 700, 97])
+def test_host_pipeline_matches_direct_forward(cuda_device, chunk_items):
+    """HostPipeline (overlapped H2D / forward / D2H), with whole batches and
+    with batches cut into item chunks, returns exactly the direct forward's output."""
     import torch
     from baidu_cti_grab_b200 import synth
     from baidu_cti_grab_b200.pipeline import HostPipeline, pack_batch
@@ -183,10 +185,12 @@ def test_host_pipeline_matches_direct_forward(cuda_device):
     rep, _, _ = _setup(torch, cuda_device, users=4, seed=26)
     cfg = synth.WorkloadConfig("pipe", 2000, "bfloat16", 40, 1, 90, "1+poisson1", 1.1)
     host = [synth.make_batch(cfg, seed=100 + i) for i in range(5)]
-    packed = [pack_batch(b) for b in host]
+    packed = [pack_batch(b, chunk_items=chunk_items) for b in host]
+    if chunk_items == 97:
+        assert all(len(pb.chunks) > 10 for pb in packed)
     outs = [torch.empty((pb.num_items, 512), dtype=torch.bfloat16).pin_memory() for pb in packed]
-    pipe = HostPipeline(rep, max_ids=max(sum(pb.lengths[:28]) for pb in packed),
-                        max_items=max(pb.num_items for pb in packed))
+    pipe = HostPipeline(rep, max_ids=max(pb.num_ids for pb in packed),
+                        max_items=max(pb.num_items for pb in packed), max_chunks=64)
     pipe.run(packed, outs)
     pipe.synchronize()
     for b, o in zip(host, outs):

@@ -1,0 +1,61 @@
+"""pack_batch cuts a batch into item chunks without changing any item's bag (CPU only)."""
+
+import numpy as np
+import pytest
+
+from baidu_cti_grab_b200 import synth
+from baidu_cti_grab_b200.pipeline import pack_batch
+
+
+def _bags(values, offsets):
+    """Reference bag semantics: bag i = values[off[i]:off[i+1]], the last bag runs to the end."""
+    n = len(offsets) - 1
+    return [values[offsets[i]:(offsets[i + 1] if i + 1 < n else len(values))] for i in range(n)]
+
+
+def _chunk_bags(pb):
+    """Per slot, the bags of every item as the packed chunks describe them."""
+    flat = pb.host.numpy()
+    S = pb.num_slots
+    out = {s: [] for s in range(1, S + 1)}
+    for ch in pb.chunks:
+        parts = np.split(flat[ch.start: ch.start + ch.size], np.cumsum(ch.lengths)[:-1])
+        for s in range(1, S + 1):
+            bags = _bags(parts[s - 1], parts[S + s - 1])
+            assert len(bags) == ch.num_items
+            out[s].extend(bags)
+    return out
+
+
+@pytest.mark.parametrize("chunk_items", [None, 1, 7, 64, 10_000])
+def test_chunks_keep_every_bag(chunk_items):
+    cfg = synth.WorkloadConfig("pack", 500, "bfloat16", 12, 1, 40, "1+poisson1", 1.1)
+    b = synth.make_batch(cfg, seed=4)
+    # trailing ids after the last offset belong to the last bag (offsets[:-1] semantics)
+    v, o = b[3]
+    b[3] = (np.concatenate([v, np.array([5, 6, 7], dtype=v.dtype)]), o)
+    pb = pack_batch(b, pin=False, chunk_items=chunk_items)
+    n = len(b[1][1]) - 1
+    assert pb.num_items == n
+    assert sum(c.num_items for c in pb.chunks) == n
+    if chunk_items:
+        assert all(c.num_items <= chunk_items for c in pb.chunks)
+    got = _chunk_bags(pb)
+    for s in range(1, 29):
+        want = _bags(np.asarray(b[s][0], dtype=np.int64), np.asarray(b[s][1], dtype=np.int64))
+        assert len(got[s]) == n
+        for g, w in zip(got[s], want):
+            assert np.array_equal(g, w)
+
+
+def test_chunking_rejects_decreasing_offsets():
+    cfg = synth.WorkloadConfig("pack", 500, "bfloat16", 8, 1, 40, "1+poisson1", 1.1)
+    b = synth.make_batch(cfg, seed=5)
+    v, o = b[2]
+    o = o.copy()
+    o[3], o[4] = o[4] + 1, o[3]
+    b[2] = (v, o)
+    with pytest.raises(ValueError):
+        pack_batch(b, pin=False, chunk_items=4)
+    pb = pack_batch(b, pin=False, chunk_items=None)  # whole batch: passed through as given
+    assert len(pb.chunks) == 1
