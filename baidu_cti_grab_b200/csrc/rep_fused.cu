@@ -319,7 +319,7 @@ __device__ __forceinline__ V sel4(const V* a, int j) {
 // thread) keeps five 7-warp CTAs resident per SM: the gather's latency needs
 // that occupancy more than the code needs registers.  An fp32 row takes 56 KB
 // of shared memory, so at most three CTAs fit and the budget is larger.
-template <typename T, int MODE, bool kFull4, typename TA>
+template <typename T, int MODE, int kS, typename TA>
 __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(const __grid_constant__ RepParams p) {
   constexpr bool kBf16 = sizeof(T) == 2;
   constexpr int kRows = kBf16 ? RB_K1_BF16_ROWS : 2;  // table rows a warp holds in registers
@@ -333,11 +333,12 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t item = blockIdx.x;
-  const int S = p.num_slots;
-  const int slot0 = warp * kSlotsPerWarp;
-  // kFull4: every warp owns exactly four slots (S % 4 == 0, e.g. the 28-slot
-  // RepEncoder), so the per-slot loops unroll with constant offsets
-  const int nsl = kFull4 ? kSlotsPerWarp : max(0, min(kSlotsPerWarp, S - slot0));
+  // kS: the slot count when known at compile time (28 for the RepEncoder), else 0
+  const int S = kS ? kS : p.num_slots;
+  // warp w owns slots 4w .. 4w+3 (fewer in the last warp when S % 4 != 0)
+  if (kS) __builtin_assume(warp < (kS + kSlotsPerWarp - 1) / kSlotsPerWarp);
+  auto slot_of = [&](int j) { return warp * kSlotsPerWarp + j; };
+  const int nsl = max(0, min(kSlotsPerWarp, S - warp * kSlotsPerWarp));
 
   // lane partials of Q_s of the warp's slots (0 for slots past S)
   float part[kSlotsPerWarp] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -351,7 +352,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
   // to T into shared memory (and the optional pooled output), then take the
   // slot statistics from the rounded values
   auto finish_slot = [&](int j, const float* acc) {
-    const int s = slot0 + j;
+    const int s = slot_of(j);
     float a0 = 0.0f, a1 = 0.0f;
     uint32_t w[8];
     F2 x[8];
@@ -416,8 +417,9 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
 
   if constexpr (MODE == kDenseLnQuant) {
 #pragma unroll
-    for (int j = 0; j < nsl; ++j) {
-      const T* xseg = reinterpret_cast<const T*>(p.xs[slot0 + j]) + item * p.ldx;
+    for (int j = 0; j < kSlotsPerWarp; ++j) {
+      if (j >= nsl) break;
+      const T* xseg = reinterpret_cast<const T*>(p.xs[slot_of(j)]) + item * p.ldx;
       float acc[16];
       if constexpr (kBf16) {
         uint32_t w[8];
@@ -445,7 +447,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     {
       const int j = lane & 3;
       if (lane < 8 && j < nsl) {
-        const int s = slot0 + j;
+        const int s = slot_of(j);
         const int64_t nz = p.slots.nnz[s];
         const int64_t* off = p.slots.offsets[s];
         const int64_t b = (lane < 4) ? off[item] : ((item + 1 < p.num_items) ? off[item + 1] : nz);
@@ -473,7 +475,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       int id = 0;
       if (t < total) {
         const int j = (t >= pre[1]) + (t >= pre[2]) + (t >= pre[3]);
-        const int64_t v = p.slots.values[slot0 + j][sel4(start, j) + (t - sel4(pre, j))];
+        const int64_t v = p.slots.values[slot_of(j)][sel4(start, j) + (t - sel4(pre, j))];
         id = (int)(v < 0 ? 0 : (v > vmax ? vmax : v));
         if (id != 0) prefetch_l2_bulk(table + (int64_t)id * kDim, kDim * (int)sizeof(T));
       }
@@ -483,7 +485,8 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     int my_id = load_window(0);
 
 #pragma unroll
-    for (int j = 0; j < nsl; ++j) {
+    for (int j = 0; j < kSlotsPerWarp; ++j) {
+      if (j >= nsl) break;
       const int tend = pre[j + 1];
       float acc[16];
 #pragma unroll
@@ -542,11 +545,11 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     const float slot_q = warp_sum4_butterfly(part[0], part[1], part[2], part[3], lane);  // lanes 8j..: slot j
     {
       const int j = lane >> 3;
-      if ((lane & 7) == 0 && j < nsl) s_q[slot0 + j] = slot_q;
+      if ((lane & 7) == 0 && j < nsl) s_q[slot_of(j)] = slot_q;
     }
     // the first slot's gamma/beta are requested before the barrier
     Affine<TA> aff;
-    if (nsl > 0) aff.load(p, slot0, lane);
+    if (nsl > 0) aff.load(p, slot_of(0), lane);
     __syncthreads();
     // every warp combines the slots itself (lane s holds slot s; lanes past S
     // contribute zero): xor-butterfly of the slot sums -> mean, then of
@@ -571,8 +574,9 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     // ---- y = fma(rstd * (x - mean), gamma, beta) rounded to T, in place; absmax
     float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < nsl; ++j) {
-      const int s = slot0 + j;
+    for (int j = 0; j < kSlotsPerWarp; ++j) {
+      if (j >= nsl) break;
+      const int s = slot_of(j);
       if (j > 0) aff.load(p, s, lane);
       if constexpr (kBf16) {
         uint32_t w[8];
@@ -623,8 +627,9 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     const bool clamp = p.act_mode == RB_ACT_STATIC;
     // ---- int8 = clamp(round_half_away(y * inv), -128, 127)
 #pragma unroll
-    for (int j = 0; j < nsl; ++j) {
-      const int s = slot0 + j;
+    for (int j = 0; j < kSlotsPerWarp; ++j) {
+      if (j >= nsl) break;
+      const int s = slot_of(j);
       F2 x[8];
       if constexpr (kBf16) {
         uint32_t w[8];
@@ -688,17 +693,17 @@ static int launch_rep(const RepParams& p, int row_dtype, cudaStream_t stream) {
   // the item's pooled row: packed bf16, or fp32 for fp32 tables
   const size_t smem = (size_t)p.num_slots * kDim * dtype_size(row_dtype);
   cudaError_t e = cudaSuccess;
-  const bool full4 = p.num_slots % kSlotsPerWarp == 0;
+  // the RepEncoder's 28 slots get a specialised kernel
+  const bool s28 = p.num_slots == 28;
   // gamma/beta storage: 16-bit words or fp32 (the pooling-only mode reads neither)
   const bool a16 = MODE != kGatherPool && p.ln_dtype != RB_F32;
   auto kern = row_dtype == RB_BF16
-                  ? (full4 ? (a16 ? rep_fused_kernel<__nv_bfloat16, MODE, true, uint16_t>
-                                  : rep_fused_kernel<__nv_bfloat16, MODE, true, float>)
-                           : (a16 ? rep_fused_kernel<__nv_bfloat16, MODE, false, uint16_t>
-                                  : rep_fused_kernel<__nv_bfloat16, MODE, false, float>))
-                  : (full4 ? (a16 ? rep_fused_kernel<float, MODE, true, uint16_t> : rep_fused_kernel<float, MODE, true, float>)
-                           : (a16 ? rep_fused_kernel<float, MODE, false, uint16_t>
-                                  : rep_fused_kernel<float, MODE, false, float>));
+                  ? (s28 ? (a16 ? rep_fused_kernel<__nv_bfloat16, MODE, 28, uint16_t>
+                                : rep_fused_kernel<__nv_bfloat16, MODE, 28, float>)
+                         : (a16 ? rep_fused_kernel<__nv_bfloat16, MODE, 0, uint16_t>
+                                : rep_fused_kernel<__nv_bfloat16, MODE, 0, float>))
+                  : (s28 ? (a16 ? rep_fused_kernel<float, MODE, 28, uint16_t> : rep_fused_kernel<float, MODE, 28, float>)
+                         : (a16 ? rep_fused_kernel<float, MODE, 0, uint16_t> : rep_fused_kernel<float, MODE, 0, float>));
   if (smem > 48 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess) kern<<<grid, block, smem, stream>>>(p);
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(rep_fused_kernel)");
