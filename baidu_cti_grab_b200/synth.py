@@ -85,7 +85,10 @@ def _affine(slot: int, rows: int) -> Tuple[int, int]:
 
 def slot_ids(rng: np.random.Generator, slot: int, rows_per_slot: int, zipf_a: float,
              count: int) -> np.ndarray:
-    """Zipf ids of one slot (1-based slot index), scattered and offset into the shared table."""
+    """Zipf ids of one slot (1-based slot index), scattered and offset into the shared table.
+    zipf_a <= 0 draws the rows uniformly instead (no hot rows: the control case)."""
+    if zipf_a <= 0:
+        return 1 + (slot - 1) * rows_per_slot + rng.integers(0, rows_per_slot, size=count, dtype=np.int64)
     z = rng.zipf(zipf_a, size=count).astype(np.int64)
     r = (z - 1) % rows_per_slot
     mult, add = _affine(slot, rows_per_slot)

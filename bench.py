@@ -56,10 +56,14 @@ def parse_args(argv=None):
     ap.add_argument("--batches", type=int, default=2, help="distinct synthetic batches cycled per rank")
     ap.add_argument("--rows-per-slot", type=int, default=None,
                     help="override table rows per slot (smaller cases for profiling captures)")
+    ap.add_argument("--uniform-ids", action="store_true",
+                    help="control run: ids drawn uniformly over each slot's rows instead of Zipf(1.1)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-chunk-items", type=int, default=None,
                     help="items per pipeline chunk on the e2e path (default: the pipeline's; 0: whole batches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm-sweep", action="store_true",
+                    help="instead of the RepEncoder step: time K2 alone for M in 1..131072 (one JSON line per M)")
     ap.add_argument("--cpu-sample-items", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     return ap.parse_args(argv)
@@ -151,6 +155,26 @@ def k2_ops(n_items: int) -> int:
 
 def k2_bytes(n_items: int) -> int:
     return n_items * H + H * D_OUT + 2 * n_items * D_OUT + 4 * n_items + D_OUT * 6
+
+
+def time_cuda(fn, reps: int = 5, warmup: int = 3, flush=None) -> float:
+    """Average device milliseconds of fn() with CUDA events (flush() runs untimed between reps)."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(reps):
+        if flush is not None:
+            flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        total += e0.elapsed_time(e1)
+    return total / reps
 
 
 # ------------------------------------------------------------- CPU baseline
@@ -283,6 +307,9 @@ def b200_arm(args):
         import dataclasses
         cfg = dataclasses.replace(cfg, rows_per_slot=args.rows_per_slot,
                                   name=f"bf16-{args.rows_per_slot}-rows-per-slot")
+    if args.uniform_ids:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, zipf_a=0.0, name=cfg.name + "-uniform-ids")
     users = cfg.num_users if args.users is None else args.users
     bf = torch.bfloat16
 
@@ -357,6 +384,12 @@ def b200_arm(args):
     k2_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / K
     assert device_ops.device_error() == 0, "device watchdog reported a timeout"
 
+    # ---- the same GEMM shape through cuBLAS int8 (torch._int_mm: int32 out, no
+    # epilogue), a measured library figure for K2 on this GPU
+    n0 = stats[0][0]
+    cublas_ms = time_cuda(lambda: torch._int_mm(q_buf[:n0], w_nk.t()), reps=5)
+    cublas_tops = k2_ops(n0) / (cublas_ms * 1e-3) / 1e12
+
     # ---- e2e through the public API from pinned host memory: packed host
     # batches, H2D / forward / D2H of successive batches overlapped on streams
     e2e = None
@@ -411,10 +444,13 @@ def b200_arm(args):
                    "frac": round(k1_gbs / hbm_peak, 4), "peak_source": peak_kind,
                    "traffic": None if k1_traffic is None else int(k1_traffic * n_mean),
                    "algorithmic_bytes": int(k1_b), "avg_ms": round(k1_ms_max, 4)}
-        roof_k2 = {"kernel": "w8a8_gemm_tc_kernel (K2 tcgen05 kind::i8)", "bound": "tensor",
+        roof_k2 = {"kernel": "w8a8_gemm_tc_pair_kernel (K2 tcgen05 kind::i8, CTA pairs)", "bound": "tensor",
                    "achieved": round(k2_tops, 1), "peak": int8_nominal, "unit": "TOP/s",
                    "frac": round(k2_tops / int8_nominal, 4), "peak_source": "nominal dense int8 (no measured figure)",
                    "frac_vs_2x_measured_bf16": round(k2_tops / (2 * bf16_peak), 4),
+                   "cublas_int8_same_shape": {"tops": round(cublas_tops, 1), "ms": round(cublas_ms, 4),
+                                              "what": "torch._int_mm, int32 out without the epilogue, rank 0"},
+                   "frac_vs_cublas_int8": round(k2_tops / cublas_tops, 4),
                    "traffic": None if k2_traffic is None else int(k2_traffic * n_mean),
                    "algorithmic_ops": int(k2_ops(int(n_mean))), "avg_ms": round(k2_ms_max, 4)}
         dominant = roof_k1 if k1_ms_max >= k2_ms_max else roof_k2
@@ -465,10 +501,57 @@ def b200_arm(args):
     return 0
 
 
+def gemm_sweep(args):
+    """K2 alone on int8 A[M, 14336] x the quantised [512, 14336] weight, bf16 out with
+    per-row / per-channel scales and bias, for M = 1 .. 131072.  An L2-sized buffer
+    is rewritten between timed launches, so every launch reads A and the weight
+    from HBM.  Small M is weight-bound (graded in GB/s), large M tensor-bound."""
+    import torch
+
+    from baidu_cti_grab_b200 import build, device_ops
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    build.build()
+    hbm_peak, _, peak_kind = measured_peaks()
+    int8_nominal = 4500.0
+    gen = torch.Generator(device=dev).manual_seed(3)
+    w = torch.randn((D_OUT, H), device=dev, generator=gen) / (H ** 0.5)
+    w_nk, w_scale = device_ops.quantize_weight_per_channel(w)
+    bias = (0.02 * torch.randn(D_OUT, device=dev, generator=gen)).to(torch.bfloat16)
+    scrub = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > L2 (126 MB)
+
+    def flush():
+        scrub.fill_(1)
+
+    for M in (1, 16, 256, 4096, 32768, 131072):
+        a = torch.randint(-127, 128, (M, H), dtype=torch.int8, device=dev, generator=gen)
+        sa = torch.rand(M, device=dev, generator=gen) * 9e-3 + 1e-3
+        out = torch.empty((M, D_OUT), dtype=torch.bfloat16, device=dev)
+        ms = time_cuda(lambda: device_ops.w8a8_gemm(a, w_nk, sa, w_scale, out, bias=bias), reps=max(3, args.steps),
+                       warmup=max(3, args.warmup), flush=flush)
+        ops, byts = k2_ops(M), k2_bytes(M)
+        line = {"metric": "w8a8 GEMM sweep", "M": M, "K": H, "N": D_OUT, "ms": round(ms, 4),
+                "tops": round(ops / (ms * 1e-3) / 1e12, 2), "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
+                "frac_int8_nominal": round(ops / (ms * 1e-3) / 1e12 / int8_nominal, 4),
+                "frac_hbm": round(byts / (ms * 1e-3) / 1e9 / hbm_peak, 4), "hbm_peak_source": peak_kind,
+                "l2": "256 MB buffer rewritten between timed launches"}
+        if M > 16:  # cuBLASLt int8 needs M > 16
+            cms = time_cuda(lambda: torch._int_mm(a, w_nk.t()), reps=max(3, args.steps), warmup=3, flush=flush)
+            line["cublas_int8_ms"] = round(cms, 4)
+            line["cublas_int8_tops"] = round(ops / (cms * 1e-3) / 1e12, 2)
+        print(json.dumps(line), flush=True)
+        del a, sa, out
+    assert device_ops.device_error() == 0, "device watchdog reported a timeout"
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return reference_arm(args)
+    if args.gemm_sweep:
+        return gemm_sweep(args)
     return b200_arm(args)
 
 

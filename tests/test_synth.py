@@ -38,3 +38,14 @@ def test_prod_config_sizes():
     n, nnz = synth.batch_stats(b)
     assert 64 <= n <= 64 * 200
     assert 1.7 * 28 * n < nnz < 2.3 * 28 * n  # mean bag size 2
+
+
+def test_uniform_ids_control_stay_in_their_slot():
+    cfg = synth.WorkloadConfig("uniform", 1000, "bfloat16", 16, 1, 20, "1+poisson1", 0.0)
+    b = synth.make_batch(cfg, seed=9)
+    for s in range(1, 29):
+        v = b[s][0]
+        assert v.min() >= 1 + (s - 1) * 1000 and v.max() <= s * 1000
+    # no hot rows: the most frequent row of a slot is rare
+    v = b[1][0]
+    assert np.bincount(v - 1).max() <= max(8, len(v) // 50)
