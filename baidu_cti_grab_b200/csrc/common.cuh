@@ -105,6 +105,47 @@ __device__ __forceinline__ float load_as_f32(const void* p, int dtype, int64_t i
   }
 }
 
+// ------------------------------------------------------------ f32x2 math
+// Blackwell packed fp32: one instruction performs two IEEE round-to-nearest
+// operations.  Lanes of a pair are independent, so results equal the scalar ops.
+struct F2 {
+  unsigned long long r;
+};
+__device__ __forceinline__ F2 f2(float lo, float hi) {
+  F2 v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v.r) : "f"(lo), "f"(hi));
+  return v;
+}
+__device__ __forceinline__ float2 un(F2 v) {
+  float2 o;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(v.r));
+  return o;
+}
+__device__ __forceinline__ F2 add2(F2 a, F2 b) {
+  F2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
+  return d;
+}
+__device__ __forceinline__ F2 sub2(F2 a, F2 b) {
+  F2 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
+  return d;
+}
+__device__ __forceinline__ F2 mul2(F2 a, F2 b) {
+  F2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
+  return d;
+}
+__device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) {
+  F2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.r) : "l"(a.r), "l"(b.r), "l"(c.r));
+  return d;
+}
+__device__ __forceinline__ F2 addrz2(F2 a, F2 b) {
+  F2 d;
+  asm("add.rz.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
+  return d;
+}
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 

@@ -134,7 +134,38 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
-// Epilogue for 32 consecutive columns of one row.
+// 32 bytes at p (32-byte aligned) in one 256-bit store: a lane fills a whole
+// 32-byte sector, although the lanes of a warp write 32 different rows
+__device__ __forceinline__ void stg_v8(void* p, const uint32_t* w) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
+// 8 consecutive per-column parameters (fp32 or 16-bit) from index i as 4 fp32 pairs
+__device__ __forceinline__ void ld_param8(const void* p, int dtype, int64_t i, F2* out) {
+  if (dtype == RB_F32) {
+    const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+    const float4 a = __ldg(q), b = __ldg(q + 1);
+    out[0] = f2(a.x, a.y); out[1] = f2(a.z, a.w); out[2] = f2(b.x, b.y); out[3] = f2(b.z, b.w);
+    return;
+  }
+  const uint4 w = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + i));
+  const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (dtype == RB_BF16) {
+      out[k] = f2(bf16_lo(ww[k]), bf16_hi(ww[k]));
+    } else {
+      const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&ww[k]));
+      out[k] = f2(h.x, h.y);
+    }
+  }
+}
+
+// Epilogue for 32 consecutive columns of one row: out = ((f32(acc) * sa) * sb) + bias,
+// one rounded fp32 operation at a time (pairs of columns per packed instruction).
+// Every array index is static, so the values stay in registers.
 __device__ __forceinline__ void epilogue_32(const uint32_t* r, int64_t row, int64_t col0, float sa_v,
                                             const EpiParams& ep) {
   const int64_t N = ep.N;
@@ -146,61 +177,78 @@ __device__ __forceinline__ void epilogue_32(const uint32_t* r, int64_t row, int6
       for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
     } else {
-      for (int j = 0; j < ncol; ++j) dst[j] = (int32_t)r[j];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncol) dst[j] = (int32_t)r[j];
     }
     return;
   }
-  float v[32];
+  const F2 sa2 = f2(sa_v, sa_v);
+  F2 v[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = mul2(f2(__int2float_rn((int)r[2 * j]), __int2float_rn((int)r[2 * j + 1])), sa2);
+  const size_t osz = ep.out_dtype == RB_F32 ? 4 : 2;
+  const bool vec = ncol == 32 && aligned(ep.sb, 16) && (ep.bias == nullptr || aligned(ep.bias, 16)) &&
+                   (col0 & 7) == 0 && ((uintptr_t)ep.out + (row * ep.ldo + col0) * osz) % 32 == 0;
+  if (vec) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      F2 p[4];
+      ld_param8(ep.sb, ep.sb_dtype, col0 + 8 * g, p);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[4 * g + k] = mul2(v[4 * g + k], p[k]);
+      if (ep.bias != nullptr) {
+        ld_param8(ep.bias, ep.bias_dtype, col0 + 8 * g, p);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[4 * g + k] = add2(v[4 * g + k], p[k]);
+      }
+    }
+    if (ep.out_dtype == RB_F32) {
+      float* dst = reinterpret_cast<float*>(ep.out) + row * ep.ldo + col0;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint32_t w[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 x = un(v[4 * g + k]);
+          w[2 * k] = __float_as_uint(x.x);
+          w[2 * k + 1] = __float_as_uint(x.y);
+        }
+        stg_v8(dst + 8 * g, w);
+      }
+    } else {
+      uint16_t* dst = reinterpret_cast<uint16_t*>(ep.out) + row * ep.ldo + col0;
+      const bool bf = ep.out_dtype == RB_BF16;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t w[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float2 x = un(v[8 * h + k]);
+          w[k] = bf ? pack_bf16x2(x.x, x.y) : pack_f16x2(x.x, x.y);
+        }
+        stg_v8(dst + 16 * h, w);
+      }
+    }
+    return;
+  }
+  // ragged or unaligned columns: element by element
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    float x = __int2float_rn((int)r[j]);
-    x = __fmul_rn(x, sa_v);
-    v[j] = x;
-  }
-  if (ncol == 32) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(v[j], load_as_f32(ep.sb, ep.sb_dtype, col0 + j));
-    if (ep.bias != nullptr) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], load_as_f32(ep.bias, ep.bias_dtype, col0 + j));
-    }
-  } else {
-    for (int j = 0; j < ncol; ++j) {
-      v[j] = __fmul_rn(v[j], load_as_f32(ep.sb, ep.sb_dtype, col0 + j));
-      if (ep.bias != nullptr) v[j] = __fadd_rn(v[j], load_as_f32(ep.bias, ep.bias_dtype, col0 + j));
-    }
-  }
-  if (ep.out_dtype == RB_F32) {
-    float* dst = reinterpret_cast<float*>(ep.out) + row * ep.ldo + col0;
-    if (ncol == 32 && aligned(dst, 16)) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    if (j >= ncol) break;
+    const float2 x2 = un(v[j >> 1]);
+    float x = (j & 1) ? x2.y : x2.x;
+    x = __fmul_rn(x, load_as_f32(ep.sb, ep.sb_dtype, col0 + j));
+    if (ep.bias != nullptr) x = __fadd_rn(x, load_as_f32(ep.bias, ep.bias_dtype, col0 + j));
+    const int64_t o = row * ep.ldo + col0 + j;
+    if (ep.out_dtype == RB_F32) {
+      reinterpret_cast<float*>(ep.out)[o] = x;
+    } else if (ep.out_dtype == RB_BF16) {
+      __nv_bfloat16 hv = __float2bfloat16_rn(x);
+      reinterpret_cast<uint16_t*>(ep.out)[o] = *reinterpret_cast<uint16_t*>(&hv);
     } else {
-      for (int j = 0; j < ncol; ++j) dst[j] = v[j];
-    }
-  } else {
-    uint16_t* dst = reinterpret_cast<uint16_t*>(ep.out) + row * ep.ldo + col0;
-    const bool bf = ep.out_dtype == RB_BF16;
-    if (ncol == 32 && aligned(dst, 16)) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 w;
-        w.x = bf ? pack_bf16x2(v[j], v[j + 1]) : pack_f16x2(v[j], v[j + 1]);
-        w.y = bf ? pack_bf16x2(v[j + 2], v[j + 3]) : pack_f16x2(v[j + 2], v[j + 3]);
-        w.z = bf ? pack_bf16x2(v[j + 4], v[j + 5]) : pack_f16x2(v[j + 4], v[j + 5]);
-        w.w = bf ? pack_bf16x2(v[j + 6], v[j + 7]) : pack_f16x2(v[j + 6], v[j + 7]);
-        *reinterpret_cast<uint4*>(dst + j) = w;
-      }
-    } else {
-      for (int j = 0; j < ncol; ++j) {
-        if (bf) {
-          __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
-          dst[j] = *reinterpret_cast<uint16_t*>(&h);
-        } else {
-          __half h = __float2half_rn(v[j]);
-          dst[j] = *reinterpret_cast<uint16_t*>(&h);
-        }
-      }
+      __half hv = __float2half_rn(x);
+      reinterpret_cast<uint16_t*>(ep.out)[o] = *reinterpret_cast<uint16_t*>(&hv);
     }
   }
 }
@@ -577,7 +625,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
-    const uint32_t tempty_leader[2] = {map_rank(smem_u32(&tempty[0]), 0), map_rank(smem_u32(&tempty[1]), 0)};
+    const uint32_t tempty_leader0 = map_rank(smem_u32(&tempty[0]), 0);
+    const uint32_t tempty_leader1 = map_rank(smem_u32(&tempty[1]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int64_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
@@ -598,7 +647,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(tempty_leader[acc]);
+      if (lane == 0) mbar_arrive_remote(acc ? tempty_leader1 : tempty_leader0);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }

@@ -60,47 +60,6 @@ struct RepParams {
   void* ln;
 };
 
-// ------------------------------------------------------------ f32x2 math
-// Blackwell packed fp32: one instruction performs two IEEE round-to-nearest
-// operations.  Lanes of a pair are independent, so results equal the scalar ops.
-struct F2 {
-  unsigned long long r;
-};
-__device__ __forceinline__ F2 f2(float lo, float hi) {
-  F2 v;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(v.r) : "f"(lo), "f"(hi));
-  return v;
-}
-__device__ __forceinline__ float2 un(F2 v) {
-  float2 o;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(v.r));
-  return o;
-}
-__device__ __forceinline__ F2 add2(F2 a, F2 b) {
-  F2 d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
-  return d;
-}
-__device__ __forceinline__ F2 sub2(F2 a, F2 b) {
-  F2 d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
-  return d;
-}
-__device__ __forceinline__ F2 mul2(F2 a, F2 b) {
-  F2 d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
-  return d;
-}
-__device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) {
-  F2 d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.r) : "l"(a.r), "l"(b.r), "l"(c.r));
-  return d;
-}
-__device__ __forceinline__ F2 addrz2(F2 a, F2 b) {
-  F2 d;
-  asm("add.rz.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
-  return d;
-}
 // bf16 pair packed in a 32-bit word (lo element in the low half) -> fp32 pair
 __device__ __forceinline__ F2 bf2(uint32_t w) { return f2(bf16_lo(w), bf16_hi(w)); }
 
