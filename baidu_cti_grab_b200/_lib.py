@@ -22,6 +22,8 @@ RB_F32, RB_BF16, RB_F16, RB_I32, RB_I8 = 0, 1, 2, 3, 4
 RB_ACT_DYNAMIC, RB_ACT_STATIC, RB_ACT_NONE = 0, 1, 2
 RB_OK, RB_ERR_VALUE, RB_ERR_UNSUPPORTED, RB_ERR_CUDA, RB_ERR_DEVICE = 0, 1, 2, 3, 4
 RB_MAX_SLOTS = 32
+RB_MAX_DEST = 8
+RB_IPC_HANDLE_BYTES = 64
 
 _vp, _i64, _i32, _f32, _u64 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_uint64
 _pp = ctypes.POINTER(ctypes.c_void_p)
@@ -47,6 +49,11 @@ SIGNATURES = {
     "rb_w8a8_gemm_workspace_size": [_i64, _i64, _i64],
     "rb_w8a8_gemm_noalloc": [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp, _i32, _vp,
                              _i64, _i32, _vp],
+    "rb_rep_gather_pool_scatter": [_vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _i64, _vp, _vp, _i32, _i64,
+                                   _vp],
+    "rb_ipc_export": [_vp, _vp, _vp],
+    "rb_ipc_import": [_vp, _i64, _vp],
+    "rb_ipc_close": [_vp, _i64],
     "rb_device_supported": [],
     "rb_device_error": [_i32],
     "rb_selftest_wait_timeout": [_u64, _vp],

@@ -4,3 +4,4 @@
 #include "rep_fused.cu"
 #include "quant.cu"
 #include "gemm_tc.cu"
+#include "peer.cu"

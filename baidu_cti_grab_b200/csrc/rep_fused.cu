@@ -58,6 +58,11 @@ struct RepParams {
   void* pooled;
   int64_t ldp;
   void* ln;
+  // pooling with scatter (num_dest > 0): item i with dest_begin[d] <= i < dest_begin[d+1]
+  // goes to dest[d] + (i - dest_begin[d])*ldp, possibly another GPU's memory
+  int num_dest;
+  void* dest[RB_MAX_DEST];
+  int64_t dest_begin[RB_MAX_DEST + 1];
 };
 
 // bf16 pair packed in a 32-bit word (lo element in the low half) -> fp32 pair
@@ -298,6 +303,18 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
   if (kS) __builtin_assume(warp < (kS + kSlotsPerWarp - 1) / kSlotsPerWarp);
   auto slot_of = [&](int j) { return warp * kSlotsPerWarp + j; };
   const int nsl = max(0, min(kSlotsPerWarp, S - warp * kSlotsPerWarp));
+  // pooling modes: start of this item's output row (its own buffer, or the
+  // receive buffer of the rank that owns the item)
+  T* out_row = nullptr;
+  if constexpr (MODE == kGatherPool) {
+    if (p.num_dest == 0) {
+      out_row = reinterpret_cast<T*>(p.pooled) + item * p.ldp;
+    } else {
+      int d = 0;
+      while (d + 1 < p.num_dest && item >= p.dest_begin[d + 1]) ++d;
+      out_row = reinterpret_cast<T*>(p.dest[d]) + (item - p.dest_begin[d]) * p.ldp;
+    }
+  }
 
   // lane partials of Q_s of the warp's slots (0 for slots past S)
   float part[kSlotsPerWarp] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -320,7 +337,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
       st_words(s_words + s * 256, lane, w);
       if constexpr (MODE == kGatherPool) {
-        st_words(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)p.slots.col_slot[s] * kDim, lane, w);
+        st_words(out_row + (int64_t)p.slots.col_slot[s] * kDim, lane, w);
       } else if (p.pooled != nullptr) {
         st_words(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, w);
       }
@@ -336,7 +353,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       for (int i = 0; i < 8; ++i) x[i] = f2(acc[2 * i], acc[2 * i + 1]);
       sts_pairs(s_f32, s, lane, x);
       if constexpr (MODE == kGatherPool) {
-        stg_pairs(reinterpret_cast<float*>(p.pooled) + item * p.ldp + (int64_t)p.slots.col_slot[s] * kDim, lane, x);
+        stg_pairs(reinterpret_cast<float*>(out_row) + (int64_t)p.slots.col_slot[s] * kDim, lane, x);
       } else if (p.pooled != nullptr) {
         stg_pairs(reinterpret_cast<float*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, x);
       }
@@ -498,6 +515,16 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     }
   }
 
+  if constexpr (MODE == kGatherPool) {
+    // rows stored into another GPU's memory are made visible system-wide before
+    // the kernel completes (the caller's barrier then hands them over): after
+    // the CTA barrier one thread's system-scope fence covers every thread's
+    // stores (fences are cumulative)
+    if (p.num_dest > 0) {
+      __syncthreads();
+      if (threadIdx.x == 0) __threadfence_system();
+    }
+  }
   if constexpr (MODE != kGatherPool) {
     const float H = (float)(S * kDim);
     const bool bf_affine = p.ln_dtype == RB_BF16;
@@ -774,6 +801,52 @@ extern "C" int rb_rep_gather_pool(const void* table, int table_dtype, int64_t nu
   p.num_items = num_items;
   p.pooled = pooled_out;
   p.ldp = ldp;
+  return launch_rep<kGatherPool>(p, table_dtype, (cudaStream_t)stream);
+}
+
+extern "C" int rb_rep_gather_pool_scatter(const void* table, int table_dtype, int64_t num_rows, int emb_dim,
+                                          const int64_t* const* slot_values, const int64_t* const* slot_offsets,
+                                          const int64_t* slot_nnz, const int* col_slot, int num_slots,
+                                          int64_t num_items, void* const* dest, const int64_t* dest_begin,
+                                          int num_dest, int64_t ld, void* stream) {
+  int rc = validate_common(num_slots, num_items);
+  if (rc) return rc;
+  if (emb_dim != kDim) return fail(RB_ERR_UNSUPPORTED, "emb_dim must be 512, got %d", emb_dim);
+  if (table_dtype != RB_BF16 && table_dtype != RB_F32)
+    return fail(RB_ERR_VALUE, "table dtype must be RB_BF16 or RB_F32");
+  if (table == nullptr || !aligned(table, 16)) return fail(RB_ERR_VALUE, "table must be 16-byte aligned");
+  if (num_rows < 1) return fail(RB_ERR_VALUE, "num_rows must be >= 1");
+  if (slot_nnz == nullptr || col_slot == nullptr) return fail(RB_ERR_VALUE, "slot_nnz/col_slot must be given");
+  if (num_dest < 1 || num_dest > RB_MAX_DEST)
+    return fail(RB_ERR_VALUE, "num_dest must be in [1, %d], got %d", RB_MAX_DEST, num_dest);
+  if (dest == nullptr || dest_begin == nullptr) return fail(RB_ERR_VALUE, "dest/dest_begin must be given");
+  if (dest_begin[0] != 0 || dest_begin[num_dest] != num_items)
+    return fail(RB_ERR_VALUE, "dest_begin must run from 0 to num_items");
+  const int esz = dtype_size(table_dtype);
+  if ((ld * esz) % 16 != 0) return fail(RB_ERR_VALUE, "ld must keep rows 16-byte aligned");
+  for (int d = 0; d < num_dest; ++d) {
+    if (dest_begin[d + 1] < dest_begin[d]) return fail(RB_ERR_VALUE, "dest_begin must not decrease");
+    if (dest_begin[d + 1] > dest_begin[d] && (dest[d] == nullptr || !aligned(dest[d], 16)))
+      return fail(RB_ERR_VALUE, "dest[%d] must be a 16-byte aligned pointer", d);
+  }
+  for (int s = 0; s < num_slots; ++s)
+    if (col_slot[s] < 0 || (int64_t)(col_slot[s] + 1) * kDim > ld)
+      return fail(RB_ERR_VALUE, "col_slot[%d]=%d does not fit in ld=%lld", s, col_slot[s], (long long)ld);
+  if (num_items == 0) return RB_OK;
+  RepParams p{};
+  rc = fill_slots(p.slots, slot_values, slot_offsets, slot_nnz, col_slot, num_slots, num_items);
+  if (rc) return rc;
+  p.table = table;
+  p.num_rows = num_rows;
+  p.num_slots = num_slots;
+  p.num_items = num_items;
+  p.ldp = ld;
+  p.num_dest = num_dest;
+  for (int d = 0; d < num_dest; ++d) {
+    p.dest[d] = dest[d];
+    p.dest_begin[d] = dest_begin[d];
+  }
+  p.dest_begin[num_dest] = dest_begin[num_dest];
   return launch_rep<kGatherPool>(p, table_dtype, (cudaStream_t)stream);
 }
 

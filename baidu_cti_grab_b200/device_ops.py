@@ -155,6 +155,52 @@ def rep_gather_pool(table: torch.Tensor, slot_values: Sequence[torch.Tensor],
     return out
 
 
+def rep_gather_pool_scatter(table: torch.Tensor, slot_values: Sequence[torch.Tensor],
+                            slot_offsets: Sequence[torch.Tensor], col_slot: Sequence[int], dest: Sequence[int],
+                            dest_begin: Sequence[int], ld: int) -> None:
+    """Gather + sum-pool of a subset of slots, item i written to the rank that owns
+    it: dest[d] + (i - dest_begin[d])*ld + col_slot[j]*512 (elements) for
+    dest_begin[d] <= i < dest_begin[d+1] (rb_rep_gather_pool_scatter).  ``dest``
+    holds raw device addresses, local or mapped from another GPU (ipc_import)."""
+    S = len(slot_values)
+    dev = require_cuda("rep_gather_pool_scatter", table, *slot_values, *slot_offsets)
+    n_items = int(slot_offsets[0].numel()) - 1
+    if len(dest) + 1 != len(dest_begin):
+        raise ValueError("dest_begin needs len(dest) + 1 entries")
+    with torch.cuda.device(dev):
+        L.call("rb_rep_gather_pool_scatter", table.data_ptr(), rb_dtype(table), table.shape[0], table.shape[1],
+               L.ptr_array([v.data_ptr() for v in slot_values]),
+               L.ptr_array([o.data_ptr() for o in slot_offsets]),
+               L.i64_array([v.numel() for v in slot_values]), L.i32_array(col_slot), S, n_items,
+               L.ptr_array(list(dest)), L.i64_array(dest_begin), len(dest), int(ld), _stream(dev))
+
+
+def ipc_export(t: torch.Tensor):
+    """(64-byte CUDA IPC handle of the allocation holding t, t's byte offset in it)."""
+    require_cuda("ipc_export", t)
+    handle = (ctypes.c_char * L.RB_IPC_HANDLE_BYTES)()
+    off = ctypes.c_int64(0)
+    with torch.cuda.device(t.device):
+        L.call("rb_ipc_export", t.data_ptr(), handle, ctypes.byref(off))
+    return bytes(handle), int(off.value)
+
+
+def ipc_import(handle: bytes, offset: int, device: torch.device) -> int:
+    """Device address, in this process, of another process's exported buffer."""
+    if len(handle) != L.RB_IPC_HANDLE_BYTES:
+        raise ValueError("an IPC handle has 64 bytes")
+    ptr = ctypes.c_void_p(0)
+    buf = (ctypes.c_char * L.RB_IPC_HANDLE_BYTES).from_buffer_copy(handle)
+    with torch.cuda.device(device):
+        L.call("rb_ipc_import", buf, int(offset), ctypes.byref(ptr))
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int, offset: int, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        L.call("rb_ipc_close", ptr, int(offset))
+
+
 def layernorm_quant(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float,
                     act_mode: str = "dynamic", static_scale: Optional[torch.Tensor] = None,
                     want_ln: bool = False):

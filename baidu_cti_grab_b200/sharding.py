@@ -16,6 +16,12 @@ Two layouts (one process per GPU, ``torch.distributed`` for the plumbing):
   slot blocks in place through per-slot row pointers (``rb_layernorm_quant_slots``)
   before the local GEMM.  The exchange is in the row dtype (bf16), exactly
   what the reference's EmbeddingBag produces, so it loses nothing.
+
+  With ``PeerExchange`` the pooling kernel does the exchange itself
+  (``rb_rep_gather_pool_scatter``): every rank maps the other ranks' receive
+  buffers (CUDA IPC) and stores each item's pooled rows straight into its
+  owner's buffer over NVLink while it pools, so the transfer overlaps the
+  gather; one small all-reduce per step then hands the rows over.
 """
 
 from __future__ import annotations
@@ -179,17 +185,51 @@ class SlotShardedRepEncoder:
         """[N_total, S_max*512] pooled rows of this rank's slots (padding columns unset)."""
         from . import device_ops
 
+        vals, offs = self._local_ids(values, offsets)
+        return device_ops.rep_gather_pool(self.table, vals, offs, list(range(len(self.plan.slots))),
+                                          self.plan.s_max)
+
+    def forward(self, values: Sequence, offsets: Sequence):
+        return self.finish(self.pool_local(values, offsets))
+
+    def _local_ids(self, values: Sequence, offsets: Sequence):
         vals, offs = [], []
         for k, s in enumerate(self.plan.slots):
             shift = ((s - 1) - k) * self.R
             v = values[s - 1]
             vals.append(v - shift if shift else v)
             offs.append(offsets[s - 1])
-        return device_ops.rep_gather_pool(self.table, vals, offs, list(range(len(self.plan.slots))),
-                                          self.plan.s_max)
+        return vals, offs
 
-    def forward(self, values: Sequence, offsets: Sequence):
-        return self.finish(self.pool_local(values, offsets))
+    def pool_scatter(self, values: Sequence, offsets: Sequence, exchange: "PeerExchange", k: int) -> None:
+        """Pool this rank's slots for all items straight into the owners' receive buffers k."""
+        from . import device_ops
+
+        vals, offs = self._local_ids(values, offsets)
+        dest, begin, ld = exchange.dest_args(k)
+        device_ops.rep_gather_pool_scatter(self.table, vals, offs, list(range(len(self.plan.slots))), dest, begin, ld)
+
+    def finish_received(self, recv):
+        """LayerNorm + int8 of this rank's items from its receive buffer [world, items, S_max*512], GEMM."""
+        from . import device_ops
+
+        torch = self._torch
+        if recv.shape[1] == 0:
+            return torch.empty((0, self.w_nk.shape[0]), dtype=recv.dtype, device=recv.device)
+        views = received_slot_views(recv, self.plan.world, recv.shape[1])
+        q, scale, _ = device_ops.layernorm_quant_slots(views, self.gamma, self.beta, self.eps)
+        out = torch.empty((q.shape[0], self.w_nk.shape[0]), dtype=recv.dtype, device=recv.device)
+        return device_ops.w8a8_gemm(q, self.w_nk, scale, self.w_scale, out, bias=self.bias)
+
+    def forward_peer(self, values: Sequence, offsets: Sequence, exchange: "PeerExchange", barrier: Callable):
+        """One step with the exchange done by the pooling kernel: pool into the
+        owners' buffers, ``barrier()`` (a collective on the current stream, e.g. an
+        NCCL all-reduce of one element), then LayerNorm + int8 + GEMM of this
+        rank's items.  Alternates between the two receive buffers."""
+        k = exchange.next_buffer()
+        self.pool_scatter(values, offsets, exchange, k)
+        barrier()
+        return self.finish_received(exchange.received(k))
 
     def finish(self, pooled):
         """Exchange, LayerNorm + int8 of this rank's items, GEMM."""
@@ -201,6 +241,78 @@ class SlotShardedRepEncoder:
         q, scale, _ = device_ops.layernorm_quant_slots(views, self.gamma, self.beta, self.eps)
         out = torch.empty((q.shape[0], self.w_nk.shape[0]), dtype=pooled.dtype, device=pooled.device)
         return device_ops.w8a8_gemm(q, self.w_nk, scale, self.w_scale, out, bias=self.bias)
+
+
+class PeerExchange:
+    """This rank's receive buffers, and every other rank's mapped into this process.
+
+    bufs[k] is [world, N_mine, S_max*512] in the row dtype: block j receives the
+    pooled rows of rank j's slots for this rank's items.  ``ptrs[k][d]`` is the
+    address of rank d's buffer k here (its own tensor for d == rank, a CUDA IPC
+    mapping otherwise).  Two buffers alternate: a rank stores step t+1's rows
+    into buffer (t+1) % 2 while the owner may still read buffer t % 2; the
+    owner's reads of buffer (t+1) % 2 from step t-1 precede its barrier of step
+    t, which every rank passes before storing step t+1.
+
+    ``all_gather_object(obj) -> list`` collects one picklable object per rank
+    (``torch.distributed.all_gather_object``); ``remote`` = None maps nothing
+    and takes ``peer_ptrs`` (for one process emulating several ranks)."""
+
+    def __init__(self, plan: SlotShardPlan, dtype, device, all_gather_object: Optional[Callable] = None,
+                 nbuf: int = 2, peer_ptrs: Optional[List[List[int]]] = None):
+        import torch
+
+        from . import device_ops
+
+        self.plan = plan
+        self.device = device
+        self.width = plan.s_max * EMB_DIM
+        self.esz = torch.empty((), dtype=dtype).element_size()
+        self.sizes = [b - a for a, b in plan.item_ranges]
+        mine = self.sizes[plan.rank]
+        self.bufs = [torch.zeros((plan.world, max(mine, 1), self.width), dtype=dtype, device=device)
+                     for _ in range(nbuf)]
+        self._opened: List[tuple] = []
+        self._step = -1
+        if peer_ptrs is not None:
+            self.ptrs = [list(p) for p in peer_ptrs]
+            return
+        if all_gather_object is None:
+            raise ValueError("PeerExchange needs all_gather_object (or peer_ptrs)")
+        exported = [device_ops.ipc_export(b) for b in self.bufs]
+        everyone = all_gather_object(exported)
+        self.ptrs = [[0] * plan.world for _ in range(nbuf)]
+        for k in range(nbuf):
+            for d in range(plan.world):
+                if d == plan.rank:
+                    self.ptrs[k][d] = self.bufs[k].data_ptr()
+                else:
+                    handle, off = everyone[d][k]
+                    ptr = device_ops.ipc_import(handle, off, device)
+                    self._opened.append((ptr, off))
+                    self.ptrs[k][d] = ptr
+
+    def received(self, k: int):
+        """This rank's rows in buffer k: [world, N_mine, S_max*512]."""
+        return self.bufs[k][:, : self.sizes[self.plan.rank]]
+
+    def next_buffer(self) -> int:
+        self._step += 1
+        return self._step % len(self.bufs)
+
+    def dest_args(self, k: int):
+        """(dest, dest_begin, ld) for rb_rep_gather_pool_scatter from this rank into buffers k."""
+        r = self.plan.rank
+        dest = [self.ptrs[k][d] + r * max(self.sizes[d], 1) * self.width * self.esz for d in range(self.plan.world)]
+        begin = [a for a, _ in self.plan.item_ranges] + [self.plan.item_ranges[-1][1]]
+        return dest, begin, self.width
+
+    def close(self) -> None:
+        from . import device_ops
+
+        for ptr, off in self._opened:
+            device_ops.ipc_close(ptr, off, self.device)
+        self._opened = []
 
 
 def build_local_table(full_table, plan: SlotShardPlan, rows_per_slot: int):

@@ -62,6 +62,10 @@ def parse_args(argv=None):
     ap.add_argument("--e2e-chunk-items", type=int, default=None,
                     help="items per pipeline chunk on the e2e path (default: the pipeline's; 0: whole batches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layout", choices=["users", "slot-sharded"], default="users",
+                    help="users: each rank a batch of its own users with a full table (the default step); "
+                         "slot-sharded: one global batch, each rank only its slots' table rows, NCCL all-to-all "
+                         "of pooled rows (the 28 x 10M-row workload)")
     ap.add_argument("--gemm-sweep", action="store_true",
                     help="instead of the RepEncoder step: time K2 alone for M in 1..131072 (one JSON line per M)")
     ap.add_argument("--cpu-sample-items", type=int, default=4096)
@@ -546,12 +550,190 @@ def gemm_sweep(args):
     return 0
 
 
+def slot_sharded_arm(args):
+    """One global batch of the large-vocabulary workload (28 slots x 10M rows =
+    287 GB of bf16 table, 4096 users, bags min(64, Zipf(1.5)), ids Zipf(1.2)).
+    Rank r holds only the rows of the slots s with (s-1) % world == r; a step is
+    gather + pool of its slots for all items, an NCCL all_to_all_single of the
+    bf16 pooled rows to the rank that owns each item range, LayerNorm + int8
+    over the received slot blocks, and the GEMM of its items.  value = items of
+    the global batch / max-over-ranks step time.  The exchange is also timed on
+    its own against the measured 770 GB/s NVLink peer bandwidth."""
+    import torch
+    import torch.distributed as dist
+
+    from baidu_cti_grab_b200 import build, device_ops, sharding, synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    if rank == 0:
+        build.build()
+    if world > 1:
+        dist.barrier()
+
+    import dataclasses
+    cfg = synth.LARGE_VOCAB_10M
+    R = args.rows_per_slot
+    if R is None:  # 10M rows per slot, or as many millions as keep the rank's table under 120 GB
+        fit = int(120e9 // (sharding.max_local_slots(world) * 1024) // 1_000_000) * 1_000_000
+        R = min(cfg.rows_per_slot, max(1_000_000, fit))
+    cfg = dataclasses.replace(cfg, rows_per_slot=R, name=f"bf16-{R // 1_000_000}M-rows-per-slot-sharded")
+    users = cfg.num_users if args.users is None else args.users
+    bf = torch.bfloat16
+    batch = synth.make_batch(cfg, seed=2000, num_users=users)  # the same global batch on every rank
+    n_total, nnz_total = synth.batch_stats(batch)
+    plan = sharding.make_slot_plan(rank, world, batch["user_offsets"])
+    table = synth.make_table_torch(1 + len(plan.slots) * R, seed=rank, dtype=bf, device=dev)
+    values, offsets = [None] * 28, [None] * 28
+    for s in plan.slots:
+        values[s - 1] = torch.from_numpy(batch[s][0]).to(dev)
+        offsets[s - 1] = torch.from_numpy(batch[s][1]).to(dev)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    gamma = (1 + 0.1 * torch.randn(H, device=dev, generator=gen)).to(bf)
+    beta = (0.1 * torch.randn(H, device=dev, generator=gen)).to(bf)
+    w = torch.randn((D_OUT, H), device=dev, generator=gen) / (H ** 0.5)
+    bias = (0.02 * torch.randn(D_OUT, device=dev, generator=gen)).to(bf)
+    w_nk, w_scale = device_ops.quantize_weight_per_channel(w)
+
+    if world > 1:
+        def all_to_all(out, inp, out_splits, in_splits):
+            dist.all_to_all_single(out, inp, out_splits, in_splits)
+    else:
+        def all_to_all(out, inp, out_splits, in_splits):
+            out.copy_(inp)
+    enc = sharding.SlotShardedRepEncoder(plan, table, R, gamma, beta, 1e-5, w_nk, w_scale, bias,
+                                         all_to_all=all_to_all)
+
+    # ---- the exchange done by the pooling kernel (stores into the owners'
+    # receive buffers over NVLink), one one-element all-reduce per step
+    exchange = sharding.PeerExchange(plan, bf, dev, all_gather_object=(
+        (lambda obj: (lambda out: (dist.all_gather_object(out, obj), out)[1])([None] * world)) if world > 1
+        else (lambda obj: [obj])))
+    flag = torch.zeros(1, dtype=torch.float32, device=dev)
+    barrier = (lambda: dist.all_reduce(flag)) if world > 1 else (lambda: None)
+
+    def run_steps(fn):
+        for _ in range(args.warmup):
+            fn(None)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(args.steps):
+            fn(ev[i])
+        t1.record()
+        torch.cuda.synchronize()
+        return (t0.elapsed_time(t1) / args.steps, sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps,
+                sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps)
+
+    def peer_step(ev):
+        k = exchange.next_buffer()
+        if ev:
+            ev[0].record()
+        enc.pool_scatter(values, offsets, exchange, k)
+        barrier()
+        if ev:
+            ev[1].record()
+        out = enc.finish_received(exchange.received(k))
+        if ev:
+            ev[2].record()
+        return out
+
+    pooled = None
+
+    def nccl_step(ev):
+        nonlocal pooled
+        if ev:
+            ev[0].record()
+        pooled = enc.pool_local(values, offsets)
+        if ev:
+            ev[1].record()
+        out = enc.finish(pooled)
+        if ev:
+            ev[2].record()
+        return out
+
+    # parity: both exchanges give this rank the same output rows
+    same = bool(torch.equal(peer_step(None), nccl_step(None)))
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms, pool_ms, finish_ms = run_steps(peer_step)
+    clock_info = clocks.stop()
+    n_ms, n_pool_ms, n_finish_ms = run_steps(nccl_step)
+
+    # the exchange alone, on the same buffers
+    width = plan.s_max * 512
+    i0, i1 = plan.my_items
+    recv = torch.empty((world, i1 - i0, width), dtype=bf, device=dev)
+    in_splits = [b - a for a, b in plan.item_ranges]
+    xch = lambda: all_to_all(recv.view(world * (i1 - i0), width), pooled, [i1 - i0] * world, in_splits)
+    if world > 1:
+        dist.barrier()
+    x_ms = time_cuda(xch, reps=5, warmup=2)
+    sent = (n_total - (i1 - i0)) * width * 2  # bytes this rank sends to the other ranks
+    assert device_ops.device_error() == 0, "device watchdog reported a timeout"
+
+    vals = torch.tensor([ms, pool_ms, finish_ms, x_ms, n_ms, n_pool_ms, n_finish_ms], dtype=torch.float64, device=dev)
+    sent_t = torch.tensor([float(sent)], dtype=torch.float64, device=dev)
+    same_t = torch.tensor([0.0 if same else 1.0], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sent_t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(same_t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    exchange.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    ms, pool_ms, finish_ms, x_ms, n_ms, n_pool_ms, n_finish_ms = [float(x) for x in vals.tolist()]
+    same = same_t.item() == 0.0
+    if rank == 0:
+        peer_gbs = 770.0
+        x_gbs = float(sent_t.item()) / (x_ms * 1e-3) / 1e9
+        line = {
+            "metric": "RepEncoder items/s (slot-sharded tables)", "value": round(n_total / (ms * 1e-3), 1),
+            "unit": "items/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": cfg.name, "users": users, "items": n_total, "ids": nnz_total,
+                       "rows_per_slot": R, "table_gb_total": round(cfg.num_rows * 1024 / 1e9, 1),
+                       "slots_per_rank": sharding.max_local_slots(world), "bags": cfg.bag, "zipf_a": cfg.zipf_a,
+                       "parallelism": f"slot-sharded x{world}, pooled bf16 rows stored to their owners over NVLink"},
+            "exchange_in": "pooling kernel (rb_rep_gather_pool_scatter: pooled rows stored into the owning "
+                           "rank's receive buffer over NVLink) + one one-element NCCL all-reduce per step",
+            "phases_ms": {"gather_pool_scatter_and_barrier": round(pool_ms, 4),
+                          "ln_quant_gemm": round(finish_ms, 4)},
+            "peer_rows_sent_per_gpu_gbs_during_pool": round(float(sent_t.item()) / (pool_ms * 1e-3) / 1e9, 1),
+            "nccl_path": {"ms_per_step": round(n_ms, 4), "items_per_s": round(n_total / (n_ms * 1e-3), 1),
+                          "phases_ms": {"gather_pool": round(n_pool_ms, 4),
+                                        "all_to_all_ln_quant_gemm": round(n_finish_ms, 4)},
+                          "all_to_all_alone": {"bytes_sent_per_gpu": int(sent_t.item()), "ms": round(x_ms, 4),
+                                               "gbs": round(x_gbs, 1), "peak": peer_gbs,
+                                               "peak_source": "measured NVLink peer copy per direction on this pool",
+                                               "frac": round(x_gbs / peer_gbs, 4)}},
+            "peer_equals_nccl": same,
+            "clocks": clock_info,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return reference_arm(args)
     if args.gemm_sweep:
         return gemm_sweep(args)
+    if args.layout == "slot-sharded":
+        return slot_sharded_arm(args)
     return b200_arm(args)
 
 

@@ -36,6 +36,7 @@ enum rb_status {
 
 /* maximum number of slots one call of the gather kernel takes */
 #define RB_MAX_SLOTS 32
+#define RB_MAX_DEST 8 /* ranks a pooled-row scatter can address */
 
 const char* rb_last_error(void);
 int rb_version(void);
@@ -95,6 +96,37 @@ int rb_rep_gather_pool(const void* table, int table_dtype, int64_t num_rows, int
                        const int64_t* const* slot_values, const int64_t* const* slot_offsets,
                        const int64_t* slot_nnz, const int* col_slot, int num_slots,
                        int64_t num_items, void* pooled_out, int64_t ldp, void* stream);
+
+/*
+ * rb_rep_gather_pool whose output rows go straight to the ranks that own the
+ * items (the pooled-row exchange of the slot-sharded multi-GPU path, done by
+ * the pooling kernel itself with stores over NVLink): item i, with
+ * dest_begin[d] <= i < dest_begin[d+1], is written at
+ * dest[d] + (i - dest_begin[d])*ld + col_slot[s]*512 (elements).  dest[d] may
+ * be another GPU's memory mapped into this process (rb_ipc_import); dest_begin
+ * holds num_dest+1 nondecreasing item indices from 0 to num_items.  The caller
+ * orders the stores before the owners read them (the kernel ends each thread
+ * with a system-scope fence; a barrier on the stream after it, e.g. an NCCL
+ * all-reduce, completes the hand-over).  The pooling follows models.py:27-34;
+ * the exchange has no counterpart in the reference, which runs on one GPU.
+ */
+int rb_rep_gather_pool_scatter(const void* table, int table_dtype, int64_t num_rows, int emb_dim,
+                               const int64_t* const* slot_values, const int64_t* const* slot_offsets,
+                               const int64_t* slot_nnz, const int* col_slot, int num_slots, int64_t num_items,
+                               void* const* dest, const int64_t* dest_begin, int num_dest, int64_t ld,
+                               void* stream);
+
+/*
+ * CUDA IPC for the scatter's destinations (no counterpart in the reference).
+ * rb_ipc_export: a 64-byte handle (RB_IPC_HANDLE_BYTES) for the device
+ * allocation that holds ptr, and ptr's byte offset in it.  rb_ipc_import, in
+ * another process on the same node: the pointer at that offset of the mapped
+ * allocation (peer access enabled).  rb_ipc_close(ptr, offset) unmaps it.
+ */
+#define RB_IPC_HANDLE_BYTES 64
+int rb_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+int rb_ipc_import(const void* handle, int64_t offset, void** ptr_out);
+int rb_ipc_close(void* ptr, int64_t offset);
 
 /*
  * LayerNorm + int8 quantisation of dense pooled rows x[num_items, ldx]

@@ -234,3 +234,49 @@ def test_slot_sharded_path_emulated_on_one_gpu(cuda_device, world):
         got = e.finish(pooled[r])
         i0, i1 = plans[r].my_items
         assert torch.equal(got, full[i0:i1])
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_pool_scatter_exchange_emulated_on_one_gpu(cuda_device, world):
+    """The slot-sharded path with the exchange done by the pooling kernel
+    (rb_rep_gather_pool_scatter), `world` ranks emulated in one process whose
+    "peer" buffers are ordinary local tensors: each rank's receive buffer equals
+    the rows the all-to-all path delivers, and its output equals the single-GPU
+    fused forward, bit for bit, over two steps (both receive buffers)."""
+    import torch
+    from baidu_cti_grab_b200 import sharding, synth
+    from baidu_cti_grab_b200.rep_encoder import rep_encoder_forward
+
+    R = 300
+    cfg = synth.WorkloadConfig("scatter", R, "bfloat16", 20, 1, 60, "1+poisson1", 1.2)
+    b = synth.make_batch(cfg, seed=41)
+    table = synth.make_table_torch(cfg.num_rows, seed=41, device=cuda_device)
+    rep, _, _ = _setup(torch, cuda_device, users=2, seed=41)
+    rep.emb.weight = torch.nn.Parameter(table, requires_grad=False)
+    values = [torch.from_numpy(b[s][0]).to(cuda_device) for s in range(1, 29)]
+    offsets = [torch.from_numpy(b[s][1]).to(cuda_device) for s in range(1, 29)]
+    full = rep_encoder_forward(rep, {s: (values[s - 1], offsets[s - 1]) for s in range(1, 29)})
+    w_nk, w_scale = rep._b200_wcache[1], rep._b200_wcache[2]
+    plans = [sharding.make_slot_plan(r, world, b["user_offsets"]) for r in range(world)]
+    encs = [sharding.SlotShardedRepEncoder(p, sharding.build_local_table(table, p, R), R, rep.input_norm.weight,
+                                           rep.input_norm.bias, 1e-5, w_nk, w_scale, rep.linear.bias,
+                                           all_to_all=lambda *a: None) for p in plans]
+    exs = [sharding.PeerExchange(p, torch.bfloat16, cuda_device, peer_ptrs=[[0] * world] * 2) for p in plans]
+    for ex in exs:
+        ex.ptrs = [[exs[d].bufs[k].data_ptr() for d in range(world)] for k in range(2)]
+    pooled = [e.pool_local(values, offsets) for e in encs]
+    for step in range(2):
+        ks = [ex.next_buffer() for ex in exs]
+        assert len(set(ks)) == 1 and ks[0] == step
+        for ex in exs:
+            ex.bufs[ks[0]].fill_(float("nan"))  # a stale row would show up
+        for r, e in enumerate(encs):
+            e.pool_scatter(values, offsets, exs[r], ks[r])
+        for r, e in enumerate(encs):
+            i0, i1 = plans[r].my_items
+            recv = exs[r].received(ks[r])
+            for j in range(world):
+                nloc = len(plans[j].slots)
+                assert torch.equal(recv[j, :, : nloc * 512], pooled[j][i0:i1, : nloc * 512])
+            got = e.finish_received(recv)
+            assert torch.equal(got, full[i0:i1])
