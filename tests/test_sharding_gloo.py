@@ -180,3 +180,30 @@ def test_dead_rank_is_detected_not_hung():
     status = res[0]
     assert isinstance(status, tuple) and status[0] == "failed", status
     assert status[1] < 60
+
+
+def test_peer_exchange_destinations():
+    """PeerExchange.dest_args: rank r's rows for rank d start at block r of d's
+    receive buffer; item boundaries are the plan's item ranges (CPU only, no IPC)."""
+    import torch
+    from baidu_cti_grab_b200 import sharding
+
+    uo = np.array([0, 5, 9, 20, 26, 40], dtype=np.int64)
+    world = 3
+    plans = [sharding.make_slot_plan(r, world, uo) for r in range(world)]
+    exs = [sharding.PeerExchange(p, torch.bfloat16, torch.device("cpu"), peer_ptrs=[[0] * world] * 2) for p in plans]
+    bases = [[1 << 40 | (d << 32) | (k << 28) for d in range(world)] for k in range(2)]
+    for ex in exs:
+        ex.ptrs = bases
+    width = plans[0].s_max * 512
+    assert exs[0].width == width
+    for r, ex in enumerate(exs):
+        assert ex.bufs[0].shape == (world, max(1, plans[r].my_items[1] - plans[r].my_items[0]), width)
+        for k in range(2):
+            dest, begin, ld = ex.dest_args(k)
+            assert ld == width
+            assert begin == [a for a, _ in plans[r].item_ranges] + [40]
+            for d in range(world):
+                n_d = plans[d].my_items[1] - plans[d].my_items[0]
+                assert dest[d] == bases[k][d] + r * max(1, n_d) * width * 2
+        assert [ex.next_buffer() for _ in range(3)] == [0, 1, 0]
