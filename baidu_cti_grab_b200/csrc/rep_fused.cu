@@ -250,6 +250,17 @@ struct Affine<float> {
   __device__ __forceinline__ F2 beta(int i, bool) const { return f2(b[2 * i], b[2 * i + 1]); }
 };
 
+// A bf16 table row of -0.0.  x + (-0.0) == x for every fp32 x (+0 and -0
+// included), so a padding id, or a position past the end of a bag, reads this
+// row and is added like any other instead of being branched around.
+#define RB_NZ4 0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u
+#define RB_NZ16 RB_NZ4, RB_NZ4, RB_NZ4, RB_NZ4
+#define RB_NZ64 RB_NZ16, RB_NZ16, RB_NZ16, RB_NZ16
+static __device__ __align__(16) const uint32_t g_negzero_row_bf16[kDim / 2] = {RB_NZ64, RB_NZ64, RB_NZ64, RB_NZ64};
+#undef RB_NZ64
+#undef RB_NZ16
+#undef RB_NZ4
+
 // Ask the copy engine to bring `bytes` at `p` into L2 (no registers, no wait).
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -480,17 +491,18 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
         }
         if constexpr (kBf16) {
           uint32_t buf[kRows][8];
+          // padding_idx 0 (and positions past the bag) add the -0.0 row: no branch
 #pragma unroll
           for (int u = 0; u < kRows; ++u)
-            if (ids[u] != 0) ldg_words(table + (int64_t)ids[u] * kDim, lane, buf[u]);
+            ldg_words(ids[u] != 0 ? static_cast<const void*>(table + (int64_t)ids[u] * kDim)
+                                  : static_cast<const void*>(g_negzero_row_bf16),
+                      lane, buf[u]);
 #pragma unroll
           for (int u = 0; u < kRows; ++u) {
-            if (ids[u] != 0) {  // padding_idx 0 is excluded; bag order kept
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                acc[2 * i] = add_lo(acc[2 * i], buf[u][i]);
-                acc[2 * i + 1] = add_hi(acc[2 * i + 1], buf[u][i]);
-              }
+            for (int i = 0; i < 8; ++i) {
+              acc[2 * i] = add_lo(acc[2 * i], buf[u][i]);
+              acc[2 * i + 1] = add_hi(acc[2 * i + 1], buf[u][i]);
             }
           }
         } else {
@@ -610,6 +622,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       inv = __fdiv_rn(1.0f, load_as_f32(p.static_scale, p.static_scale_dtype, 0));
     }
     const F2 inv2 = f2(inv, inv);
+    int8_t* const q_lane = p.q + item * p.ldq + 8 * lane;  // this lane's columns of the item's int8 row
     const bool clamp = p.act_mode == RB_ACT_STATIC;
     // ---- int8 = clamp(round_half_away(y * inv), -128, 127)
 #pragma unroll
@@ -636,7 +649,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
         }
         round_half_away2(v, q[2 * i], q[2 * i + 1]);
       }
-      int8_t* dst = p.q + item * p.ldq + (int64_t)s * kDim + 8 * lane;
+      int8_t* dst = q_lane + s * kDim;
       *reinterpret_cast<uint2*>(dst) = make_uint2(pack_i8x4_prmt(q[0], q[1], q[2], q[3]),
                                                   pack_i8x4_prmt(q[4], q[5], q[6], q[7]));
       *reinterpret_cast<uint2*>(dst + 256) = make_uint2(pack_i8x4_prmt(q[8], q[9], q[10], q[11]),
