@@ -146,6 +146,14 @@ __device__ __forceinline__ F2 addrz2(F2 a, F2 b) {
   asm("add.rz.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
   return d;
 }
+// 32 bytes at p (32-byte aligned) in one 256-bit store: a lane fills a whole
+// 32-byte sector with one instruction
+__device__ __forceinline__ void stg_v8(void* p, const uint32_t* w) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 

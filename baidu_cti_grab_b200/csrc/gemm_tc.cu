@@ -134,14 +134,6 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
-// 32 bytes at p (32-byte aligned) in one 256-bit store: a lane fills a whole
-// 32-byte sector, although the lanes of a warp write 32 different rows
-__device__ __forceinline__ void stg_v8(void* p, const uint32_t* w) {
-  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]),
-               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
-               : "memory");
-}
-
 // 8 consecutive per-column parameters (fp32 or 16-bit) from index i as 4 fp32 pairs
 __device__ __forceinline__ void ld_param8(const void* p, int dtype, int64_t i, F2* out) {
   if (dtype == RB_F32) {

@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
       st_words(s_words + s * 256, lane, w);
       if constexpr (MODE == kGatherPool) {
-        st_words(out_row + (int64_t)p.slots.col_slot[s] * kDim, lane, w);
+        if (p.num_dest == 0) st_words(out_row + (int64_t)p.slots.col_slot[s] * kDim, lane, w);
       } else if (p.pooled != nullptr) {
         st_words(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, w);
       }
@@ -527,14 +527,22 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     }
   }
 
-  if constexpr (MODE == kGatherPool) {
-    // rows stored into another GPU's memory are made visible system-wide before
-    // the kernel completes (the caller's barrier then hands them over): after
-    // the CTA barrier one thread's system-scope fence covers every thread's
-    // stores (fences are cumulative)
+  if constexpr (MODE == kGatherPool && kBf16) {
     if (p.num_dest > 0) {
+      // scatter: the item's pooled bf16 row is complete in shared memory; copy
+      // it to its owner 32 bytes per thread per step (a warp writes 1 KB per
+      // store instruction), so the rows cross NVLink in whole sectors.  No
+      // fence: the stores happen before the kernel's completion, which happens
+      // before the caller's barrier (a collective on the same stream) whose
+      // cross-GPU release/acquire publishes them to the owner.
       __syncthreads();
-      if (threadIdx.x == 0) __threadfence_system();
+      for (int c = threadIdx.x; c < S * 32; c += blockDim.x) {
+        const int s = c >> 5, k = c & 31;
+        const uint4* src = reinterpret_cast<const uint4*>(s_words + s * 256) + 2 * k;
+        const uint4 a = src[0], b = src[1];
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        stg_v8(out_row + (int64_t)p.slots.col_slot[s] * kDim + 16 * k, w);
+      }
     }
   }
   if constexpr (MODE != kGatherPool) {
@@ -836,11 +844,13 @@ extern "C" int rb_rep_gather_pool_scatter(const void* table, int table_dtype, in
   if (dest_begin[0] != 0 || dest_begin[num_dest] != num_items)
     return fail(RB_ERR_VALUE, "dest_begin must run from 0 to num_items");
   const int esz = dtype_size(table_dtype);
-  if ((ld * esz) % 16 != 0) return fail(RB_ERR_VALUE, "ld must keep rows 16-byte aligned");
+  // bf16 rows leave in 32-byte stores, fp32 rows in 16-byte stores
+  const int row_align = table_dtype == RB_BF16 ? 32 : 16;
+  if ((ld * esz) % row_align != 0) return fail(RB_ERR_VALUE, "ld must keep rows %d-byte aligned", row_align);
   for (int d = 0; d < num_dest; ++d) {
     if (dest_begin[d + 1] < dest_begin[d]) return fail(RB_ERR_VALUE, "dest_begin must not decrease");
-    if (dest_begin[d + 1] > dest_begin[d] && (dest[d] == nullptr || !aligned(dest[d], 16)))
-      return fail(RB_ERR_VALUE, "dest[%d] must be a 16-byte aligned pointer", d);
+    if (dest_begin[d + 1] > dest_begin[d] && (dest[d] == nullptr || !aligned(dest[d], row_align)))
+      return fail(RB_ERR_VALUE, "dest[%d] must be a %d-byte aligned pointer", d, row_align);
   }
   for (int s = 0; s < num_slots; ++s)
     if (col_slot[s] < 0 || (int64_t)(col_slot[s] + 1) * kDim > ld)

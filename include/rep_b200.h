@@ -104,10 +104,12 @@ int rb_rep_gather_pool(const void* table, int table_dtype, int64_t num_rows, int
  * dest_begin[d] <= i < dest_begin[d+1], is written at
  * dest[d] + (i - dest_begin[d])*ld + col_slot[s]*512 (elements).  dest[d] may
  * be another GPU's memory mapped into this process (rb_ipc_import); dest_begin
- * holds num_dest+1 nondecreasing item indices from 0 to num_items.  The caller
- * orders the stores before the owners read them (the kernel ends each thread
- * with a system-scope fence; a barrier on the stream after it, e.g. an NCCL
- * all-reduce, completes the hand-over).  The pooling follows models.py:27-34;
+ * holds num_dest+1 nondecreasing item indices from 0 to num_items; dest rows
+ * must be 32-byte aligned (ld*2 a multiple of 32 bytes) for bf16 tables.  The
+ * caller hands the rows over with a barrier on the same stream after the call,
+ * e.g. an NCCL all-reduce: the kernel's stores happen before its completion,
+ * and the barrier's cross-GPU release/acquire publishes them to the owners.
+ * The pooling follows models.py:27-34;
  * the exchange has no counterpart in the reference, which runs on one GPU.
  */
 int rb_rep_gather_pool_scatter(const void* table, int table_dtype, int64_t num_rows, int emb_dim,
