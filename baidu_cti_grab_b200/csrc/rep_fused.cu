@@ -63,6 +63,7 @@ struct RepParams {
   int num_dest;
   void* dest[RB_MAX_DEST];
   int64_t dest_begin[RB_MAX_DEST + 1];
+  int64_t item_shift;  // CTA b pools item (b + item_shift) % num_items
 };
 
 // bf16 pair packed in a 32-bit word (lo element in the low half) -> fp32 pair
@@ -307,7 +308,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int64_t item = blockIdx.x;
+  const int64_t item = p.item_shift == 0 ? (int64_t)blockIdx.x : ((int64_t)blockIdx.x + p.item_shift) % p.num_items;
   // kS: the slot count when known at compile time (28 for the RepEncoder), else 0
   const int S = kS ? kS : p.num_slots;
   // warp w owns slots 4w .. 4w+3 (fewer in the last warp when S % 4 != 0)
@@ -829,7 +830,7 @@ extern "C" int rb_rep_gather_pool_scatter(const void* table, int table_dtype, in
                                           const int64_t* const* slot_values, const int64_t* const* slot_offsets,
                                           const int64_t* slot_nnz, const int* col_slot, int num_slots,
                                           int64_t num_items, void* const* dest, const int64_t* dest_begin,
-                                          int num_dest, int64_t ld, void* stream) {
+                                          int num_dest, int64_t ld, int64_t item_shift, void* stream) {
   int rc = validate_common(num_slots, num_items);
   if (rc) return rc;
   if (emb_dim != kDim) return fail(RB_ERR_UNSUPPORTED, "emb_dim must be 512, got %d", emb_dim);
@@ -856,6 +857,7 @@ extern "C" int rb_rep_gather_pool_scatter(const void* table, int table_dtype, in
     if (col_slot[s] < 0 || (int64_t)(col_slot[s] + 1) * kDim > ld)
       return fail(RB_ERR_VALUE, "col_slot[%d]=%d does not fit in ld=%lld", s, col_slot[s], (long long)ld);
   if (num_items == 0) return RB_OK;
+  if (item_shift < 0 || item_shift >= num_items) return fail(RB_ERR_VALUE, "item_shift must be in [0, num_items)");
   RepParams p{};
   rc = fill_slots(p.slots, slot_values, slot_offsets, slot_nnz, col_slot, num_slots, num_items);
   if (rc) return rc;
@@ -864,6 +866,7 @@ extern "C" int rb_rep_gather_pool_scatter(const void* table, int table_dtype, in
   p.num_slots = num_slots;
   p.num_items = num_items;
   p.ldp = ld;
+  p.item_shift = item_shift;
   p.num_dest = num_dest;
   for (int d = 0; d < num_dest; ++d) {
     p.dest[d] = dest[d];

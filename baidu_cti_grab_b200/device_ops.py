@@ -157,11 +157,12 @@ def rep_gather_pool(table: torch.Tensor, slot_values: Sequence[torch.Tensor],
 
 def rep_gather_pool_scatter(table: torch.Tensor, slot_values: Sequence[torch.Tensor],
                             slot_offsets: Sequence[torch.Tensor], col_slot: Sequence[int], dest: Sequence[int],
-                            dest_begin: Sequence[int], ld: int) -> None:
+                            dest_begin: Sequence[int], ld: int, item_shift: int = 0) -> None:
     """Gather + sum-pool of a subset of slots, item i written to the rank that owns
     it: dest[d] + (i - dest_begin[d])*ld + col_slot[j]*512 (elements) for
     dest_begin[d] <= i < dest_begin[d+1] (rb_rep_gather_pool_scatter).  ``dest``
-    holds raw device addresses, local or mapped from another GPU (ipc_import)."""
+    holds raw device addresses, local or mapped from another GPU (ipc_import).
+    Items are processed from ``item_shift`` on, wrapping around."""
     S = len(slot_values)
     dev = require_cuda("rep_gather_pool_scatter", table, *slot_values, *slot_offsets)
     n_items = int(slot_offsets[0].numel()) - 1
@@ -172,7 +173,8 @@ def rep_gather_pool_scatter(table: torch.Tensor, slot_values: Sequence[torch.Ten
                L.ptr_array([v.data_ptr() for v in slot_values]),
                L.ptr_array([o.data_ptr() for o in slot_offsets]),
                L.i64_array([v.numel() for v in slot_values]), L.i32_array(col_slot), S, n_items,
-               L.ptr_array(list(dest)), L.i64_array(dest_begin), len(dest), int(ld), _stream(dev))
+               L.ptr_array(list(dest)), L.i64_array(dest_begin), len(dest), int(ld),
+               int(item_shift) if n_items else 0, _stream(dev))
 
 
 def ipc_export(t: torch.Tensor):

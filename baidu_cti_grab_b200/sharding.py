@@ -207,7 +207,11 @@ class SlotShardedRepEncoder:
 
         vals, offs = self._local_ids(values, offsets)
         dest, begin, ld = exchange.dest_args(k)
-        device_ops.rep_gather_pool_scatter(self.table, vals, offs, list(range(len(self.plan.slots))), dest, begin, ld)
+        # start at the next rank's items: at any moment the ranks store into different owners
+        n = begin[-1]
+        shift = begin[(self.plan.rank + 1) % self.plan.world] % n if n else 0
+        device_ops.rep_gather_pool_scatter(self.table, vals, offs, list(range(len(self.plan.slots))), dest, begin, ld,
+                                           item_shift=shift)
 
     def finish_received(self, recv):
         """LayerNorm + int8 of this rank's items from its receive buffer [world, items, S_max*512], GEMM."""

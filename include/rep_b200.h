@@ -109,14 +109,16 @@ int rb_rep_gather_pool(const void* table, int table_dtype, int64_t num_rows, int
  * caller hands the rows over with a barrier on the same stream after the call,
  * e.g. an NCCL all-reduce: the kernel's stores happen before its completion,
  * and the barrier's cross-GPU release/acquire publishes them to the owners.
- * The pooling follows models.py:27-34;
+ * Items are taken in the order item_shift, item_shift+1, ... (mod num_items):
+ * ranks that start at different owners' ranges keep every NVLink busy instead
+ * of all storing into one owner at a time.  The pooling follows models.py:27-34;
  * the exchange has no counterpart in the reference, which runs on one GPU.
  */
 int rb_rep_gather_pool_scatter(const void* table, int table_dtype, int64_t num_rows, int emb_dim,
                                const int64_t* const* slot_values, const int64_t* const* slot_offsets,
                                const int64_t* slot_nnz, const int* col_slot, int num_slots, int64_t num_items,
                                void* const* dest, const int64_t* dest_begin, int num_dest, int64_t ld,
-                               void* stream);
+                               int64_t item_shift, void* stream);
 
 /*
  * CUDA IPC for the scatter's destinations (no counterpart in the reference).
