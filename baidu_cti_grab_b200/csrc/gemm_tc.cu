@@ -684,6 +684,94 @@ __global__ void splitk_finalize_kernel(const __grid_constant__ EpiParams ep) {
   }
 }
 
+// out[m, n] = epilogue(acc) for one element (the finalize and small-M paths)
+__device__ __forceinline__ void epilogue_one(int32_t acc, int64_t m, int64_t n, const EpiParams& ep) {
+  if (ep.out_dtype == RB_I32) {
+    reinterpret_cast<int32_t*>(ep.out)[m * ep.ldo + n] = acc;
+    return;
+  }
+  float v = __int2float_rn(acc);
+  v = __fmul_rn(v, load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? m : 0));
+  v = __fmul_rn(v, load_as_f32(ep.sb, ep.sb_dtype, n));
+  if (ep.bias != nullptr) v = __fadd_rn(v, load_as_f32(ep.bias, ep.bias_dtype, n));
+  if (ep.out_dtype == RB_F32) {
+    reinterpret_cast<float*>(ep.out)[m * ep.ldo + n] = v;
+  } else if (ep.out_dtype == RB_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(ep.out)[m * ep.ldo + n] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<__half*>(ep.out)[m * ep.ldo + n] = __float2half_rn(v);
+  }
+}
+
+// Small M (M <= kGemvMaxM): reading the [N, K] weight once is the whole cost,
+// and a tensor-core tile would be 1/8 full.  One launch, no workspace: a CTA
+// owns kGemvCols output columns; its threads stride over the 16-byte K chunks,
+// each chunk of B read once (coalesced) and dotted with the same chunk of every
+// row of A through dp4a (exact int32 products and sums); the partial sums meet
+// through warp shuffles and shared memory, then the usual epilogue.  int32
+// addition (modulo 2^32, like the tensor core's) is associative, so the result
+// equals the tiled kernels' bit for bit.
+constexpr int kGemvMaxM = 16;
+constexpr int kGemvCols = 4;
+constexpr int kGemvThreads = 256;
+template <int MT>
+__global__ void __launch_bounds__(kGemvThreads, 1)
+    w8a8_gemv_kernel(const int8_t* __restrict__ A, int64_t lda, const int8_t* __restrict__ B, int64_t ldb,
+                     const __grid_constant__ EpiParams ep) {
+  __shared__ uint32_t red[kGemvThreads / 32][MT * kGemvCols];
+  const int64_t n0 = (int64_t)blockIdx.x * kGemvCols;
+  const int M = (int)ep.M;
+  const int64_t chunks = ep.K / 16;
+  int32_t acc[MT][kGemvCols];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int c = 0; c < kGemvCols; ++c) acc[m][c] = 0;
+  for (int64_t q = threadIdx.x; q < chunks; q += kGemvThreads) {
+    // every load of the chunk first (one memory round trip), then the dot products
+    int4 b[kGemvCols], a[MT];
+#pragma unroll
+    for (int c = 0; c < kGemvCols; ++c)
+      b[c] = (n0 + c < ep.N) ? __ldg(reinterpret_cast<const int4*>(B + (n0 + c) * ldb) + q) : make_int4(0, 0, 0, 0);
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+      a[m] = m < M ? __ldg(reinterpret_cast<const int4*>(A + m * lda) + q) : make_int4(0, 0, 0, 0);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+#pragma unroll
+      for (int c = 0; c < kGemvCols; ++c) {
+        int v = acc[m][c];
+        v = __dp4a(a[m].x, b[c].x, v);
+        v = __dp4a(a[m].y, b[c].y, v);
+        v = __dp4a(a[m].z, b[c].z, v);
+        v = __dp4a(a[m].w, b[c].w, v);
+        acc[m][c] = v;
+      }
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+#pragma unroll
+    for (int c = 0; c < kGemvCols; ++c) {
+      uint32_t v = (uint32_t)acc[m][c];
+#pragma unroll
+      for (int d = 16; d >= 1; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+      if (lane == 0) red[warp][m * kGemvCols + c] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < MT * kGemvCols) {
+    const int m = threadIdx.x / kGemvCols, c = threadIdx.x % kGemvCols;
+    if (m < M && n0 + c < ep.N) {
+      uint32_t sum = 0;
+#pragma unroll
+      for (int w = 0; w < kGemvThreads / 32; ++w) sum += red[w][threadIdx.x];
+      epilogue_one((int32_t)sum, m, n0 + c, ep);
+    }
+  }
+}
+
 // CUDA-core GEMM for shapes the tensor-map path cannot take (K % 16 != 0,
 // unaligned operands, K == 0).  One thread per output element.
 __global__ void w8a8_gemm_simple_kernel(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
@@ -754,7 +842,7 @@ using namespace rb;
 // cover the SMs, at least two K blocks per split
 static int choose_ksplits(int64_t M, int64_t N, int64_t K) {
   using namespace rb::tc;
-  if (M >= RB_GEMM_PAIR_MIN_M || K <= 0 || K % 16 != 0) return 1;
+  if (M >= RB_GEMM_PAIR_MIN_M || M <= tc::kGemvMaxM || K <= 0 || K % 16 != 0) return 1;
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int64_t kblocks = (K + BK - 1) / BK;
   int64_t s = std::min<int64_t>(sm_count() / std::max<int64_t>(tiles, 1), kblocks / 2);
@@ -811,6 +899,15 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
     const int threads = 256;
     w8a8_gemm_simple_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(A, lda, B, ldb, ep);
     return check_cuda(cudaGetLastError(), "w8a8_gemm_simple_kernel launch");
+  }
+  if (M <= kGemvMaxM) {
+    const unsigned grid = (unsigned)((N + kGemvCols - 1) / kGemvCols);
+    if (M <= 1) w8a8_gemv_kernel<1><<<grid, kGemvThreads, 0, st>>>(A, lda, B, ldb, ep);
+    else if (M <= 2) w8a8_gemv_kernel<2><<<grid, kGemvThreads, 0, st>>>(A, lda, B, ldb, ep);
+    else if (M <= 4) w8a8_gemv_kernel<4><<<grid, kGemvThreads, 0, st>>>(A, lda, B, ldb, ep);
+    else if (M <= 8) w8a8_gemv_kernel<8><<<grid, kGemvThreads, 0, st>>>(A, lda, B, ldb, ep);
+    else w8a8_gemv_kernel<16><<<grid, kGemvThreads, 0, st>>>(A, lda, B, ldb, ep);
+    return check_cuda(cudaGetLastError(), "w8a8_gemv_kernel launch");
   }
   int dev = 0;
   cudaGetDevice(&dev);

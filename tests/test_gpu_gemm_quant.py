@@ -196,7 +196,35 @@ def test_watchdog_timeout_status(cuda_device):
     assert float(x.sum()) == 4.0
 
 
-@pytest.mark.parametrize("M", [1, 16, 256, 700])
+@pytest.mark.parametrize("M,N", [(1, 512), (2, 512), (3, 512), (5, 256), (8, 512), (13, 520), (16, 512)])
+@pytest.mark.parametrize("out_name", ["bf16", "f32", "i32"])
+def test_gemm_small_m_equals_tensor_core_rows(cuda_device, M, N, out_name):
+    """M <= 16 runs the dp4a kernel (one launch, no workspace): its rows equal the
+    same rows computed by the tensor-core kernel inside a larger M, bit for bit,
+    and its int32 accumulators equal an fp64 matmul."""
+    import torch
+    from baidu_cti_grab_b200 import _lib as L, device_ops
+
+    K = 14336
+    assert L.load().rb_w8a8_gemm_workspace_size(M, N, K) == 0
+    gen = torch.Generator(device=cuda_device).manual_seed(100 + M)
+    a = torch.randint(-128, 128, (40, K), dtype=torch.int8, device=cuda_device, generator=gen)
+    b = torch.randint(-128, 128, (N, K), dtype=torch.int8, device=cuda_device, generator=gen)
+    sa = torch.rand(40, device=cuda_device, generator=gen) * 1e-2
+    sb = torch.rand(N, device=cuda_device, generator=gen) * 1e-2
+    bias = torch.randn(N, device=cuda_device, generator=gen).to(torch.bfloat16)
+    dt = {"bf16": torch.bfloat16, "f32": torch.float32, "i32": torch.int32}[out_name]
+    raw = dt == torch.int32
+    big = device_ops.w8a8_gemm(a, b, None if raw else sa, None if raw else sb,
+                               torch.empty((40, N), dtype=dt, device=cuda_device), bias=None if raw else bias)
+    small = device_ops.w8a8_gemm(a[:M], b, None if raw else sa[:M], None if raw else sb,
+                                 torch.empty((M, N), dtype=dt, device=cuda_device), bias=None if raw else bias)
+    assert torch.equal(small, big[:M])
+    acc = device_ops.w8a8_gemm(a[:M], b, None, None, torch.empty((M, N), dtype=torch.int32, device=cuda_device))
+    assert torch.equal(acc.double(), a[:M].double() @ b.double().t())
+
+
+@pytest.mark.parametrize("M", [17, 256, 700])
 def test_gemm_split_k_equals_unsplit(cuda_device, M):
     """The split-K path (workspace given) and the unsplit kernel (rb_w8a8_gemm) agree bit for bit."""
     import torch
