@@ -23,8 +23,9 @@
 //               buffer so the MMA warp overlaps the next tile's main loop.
 // For M >= RB_GEMM_PAIR_MIN_M a two-SM variant (namespace pair) runs each
 // 256x256 tile on a cluster of two CTAs with tcgen05.mma.cta_group::2; for
-// small M the one-SM kernel splits K across CTAs into an int32 workspace that
-// splitk_finalize_kernel sums in split order.  No TMA load carries a cluster
+// 17 <= M with fewer tiles than SMs the one-SM kernel splits K across CTAs
+// into an int32 workspace that splitk_finalize_kernel sums in split order; for
+// M <= 16 w8a8_gemv_kernel uses dp4a on the CUDA cores.  No TMA load carries a cluster
 // multicast (only tcgen05.commit signals both CTAs of a pair).  Every mbarrier
 // wait is bounded (common.cuh): on timeout the kernel records a watchdog code,
 // drains what it issued and returns instead of hanging.

@@ -187,7 +187,9 @@ int rb_pack_weight_nk(const int8_t* src, int64_t K, int64_t N, int64_t stride_k,
  * or the raw int32 acc when out_dtype == RB_I32 (scales/bias ignored).
  * Replaces quantization/w8a8_triton_kernels.py:174-318,470-640
  * (w8a8_scaled_mm[_out], int8_mm_no_scale[_out]) and kernels/quantization.py:38-105
- * (_w8a8_matmul_kernel).  tcgen05 kind::i8 on sm_100a with the accumulator in TMEM.
+ * (_w8a8_matmul_kernel).  tcgen05 kind::i8 on sm_100a with the accumulator in TMEM
+ * (one-SM tiles; CTA-pair tiles for M >= 16384); M <= 16 uses int8 dot products
+ * on the CUDA cores (one launch), with the same results bit for bit.
  *   A     int8 [M, lda]  (K contiguous; lda % 16 == 0, 16-byte aligned)
  *   B     int8 [N, ldb]  (K contiguous; ldb % 16 == 0, 16-byte aligned)
  *   sa    per-row [M] (sa_per_row=1) or scalar [1]; sa_dtype RB_F32/RB_BF16/RB_F16
@@ -200,8 +202,8 @@ int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int
                  int out_dtype, void* stream);
 
 /*
- * rb_w8a8_gemm with a caller-provided int32 workspace: for small M (fewer
- * output tiles than SMs) the K dimension is split across CTAs, each split's
+ * rb_w8a8_gemm with a caller-provided int32 workspace: for small M (17 <= M and
+ * fewer output tiles than SMs) the K dimension is split across CTAs, each split's
  * int32 partial goes to the workspace, and a second kernel sums the splits in
  * split order (exact) and applies the epilogue.  Same results as rb_w8a8_gemm,
  * bit for bit.  rb_w8a8_gemm_workspace_size(M, N, K) gives the number of int32
