@@ -312,6 +312,9 @@ class PeerExchange:
         return dest, begin, self.width
 
     def close(self) -> None:
+        """Unmap the other ranks' buffers.  Call it on every rank after a barrier
+        that follows the last step (no rank may still be storing into a buffer
+        that its owner frees), and before the ranks exit."""
         from . import device_ops
 
         for ptr, off in self._opened:
