@@ -280,3 +280,28 @@ def test_pool_scatter_exchange_emulated_on_one_gpu(cuda_device, world):
                 assert torch.equal(recv[j, :, : nloc * 512], pooled[j][i0:i1, : nloc * 512])
             got = e.finish_received(recv)
             assert torch.equal(got, full[i0:i1])
+
+
+def test_pool_scatter_fp32_table_matches_pool(cuda_device):
+    """rb_rep_gather_pool_scatter with an fp32 table (rows stored slot by slot,
+    not through the shared-memory row copy) and items taken from a shifted
+    start: every destination row equals rb_rep_gather_pool's, bit for bit."""
+    import torch
+    from baidu_cti_grab_b200 import device_ops, synth
+
+    cfg = synth.WorkloadConfig("scatter32", 200, "float32", 12, 1, 30, "uniform1-4", 1.1)
+    b = synth.make_batch(cfg, seed=7)
+    table = torch.from_numpy(synth.make_table_numpy(cfg.num_rows, seed=7, dtype="float32")).to(cuda_device)
+    slots = [3, 11, 20]
+    vals = [torch.from_numpy(b[s][0]).to(cuda_device) for s in slots]
+    offs = [torch.from_numpy(b[s][1]).to(cuda_device) for s in slots]
+    n = len(b[1][1]) - 1
+    width = 4 * 512
+    ref = device_ops.rep_gather_pool(table, vals, offs, [0, 1, 2], 4)
+    cut = [0, n // 3, (2 * n) // 3, n]
+    bufs = [torch.full((max(1, cut[d + 1] - cut[d]), width), float("nan"), device=cuda_device) for d in range(3)]
+    device_ops.rep_gather_pool_scatter(table, vals, offs, [0, 1, 2], [t.data_ptr() for t in bufs], cut, width,
+                                       item_shift=cut[2])
+    for d in range(3):
+        rows = cut[d + 1] - cut[d]
+        assert torch.equal(bufs[d][:rows, : 3 * 512], ref[cut[d]:cut[d + 1], : 3 * 512])
