@@ -59,3 +59,12 @@ def test_chunking_rejects_decreasing_offsets():
         pack_batch(b, pin=False, chunk_items=4)
     pb = pack_batch(b, pin=False, chunk_items=None)  # whole batch: passed through as given
     assert len(pb.chunks) == 1
+
+
+def test_empty_batch_packs_as_one_empty_chunk():
+    b = {"user_offsets": np.zeros(1, dtype=np.int64)}
+    for s in range(1, 29):
+        b[s] = (np.zeros(0, dtype=np.int64), np.zeros(1, dtype=np.int64))
+    pb = pack_batch(b, pin=False, chunk_items=4)
+    assert pb.num_items == 0 and pb.num_ids == 0 and len(pb.chunks) == 1
+    assert pb.chunks[0].num_items == 0 and pb.host.numel() == 28  # 28 one-entry offset arrays
