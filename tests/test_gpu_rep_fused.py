@@ -140,36 +140,45 @@ def test_k1_affine_param_dtypes_on_bf16_rows(cuda_device, param_dtype, offset):
     assert np.array_equal(scale.cpu().numpy(), oscale)
 
 
-def test_k1_edge_cases(cuda_device):
-    """Zero items, one item, every bag empty, ids out of range / negative / padding."""
+@pytest.mark.parametrize("dt,S", [("float32", 28), ("bfloat16", 28), ("bfloat16", 5), ("bfloat16", 32),
+                                  ("float32", 7)])
+def test_k1_edge_cases(cuda_device, dt, S):
+    """Zero items, one item, every bag empty, ids out of range / negative / padding,
+    bags longer than the 32-id window, odd bag lengths; bf16 and fp32 tables, the
+    28-slot kernel and the generic slot count (5, 7 and the maximum 32)."""
     import torch
     from oracle import oracle as O
     from baidu_cti_grab_b200 import device_ops
 
     dev = cuda_device
     V = 40
-    table_np = (np.random.default_rng(0).standard_normal((V, 512)) * 0.02).astype(np.float32)
-    table = torch.from_numpy(table_np).to(dev)
-    g = torch.ones(28 * 512, device=dev)
-    b = torch.zeros(28 * 512, device=dev)
+    H = S * 512
+    t32 = (np.random.default_rng(0).standard_normal((V, 512)) * 0.02).astype(np.float32)
+    table_np = O.f32_to_bf16_bits(t32) if dt == "bfloat16" else t32
+    table = _table_tensor(torch, table_np, dt, dev)
+    tdt = torch.bfloat16 if dt == "bfloat16" else torch.float32
+    g = torch.ones(H, device=dev, dtype=tdt)
+    b = torch.zeros(H, device=dev, dtype=tdt)
     # zero items
-    vals = [torch.zeros(0, dtype=torch.int64, device=dev) for _ in range(28)]
-    offs = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(28)]
+    vals = [torch.zeros(0, dtype=torch.int64, device=dev) for _ in range(S)]
+    offs = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(S)]
     q, s, _, _ = device_ops.rep_gather_ln_quant(table, vals, offs, g, b, 1e-5)
-    assert q.shape == (0, 28 * 512)
-    # three items: all bags empty for item 0, item 1 has odd ids, item 2 long bags
-    batch = {"user_offsets": np.array([0, 3])}
+    assert q.shape == (0, H)
+    # four items: all bags empty for item 0, item 1 has odd ids (padding, negative,
+    # past the vocabulary), item 2 a 40-id bag, item 3 a 3-id bag (odd length)
+    batch = {"user_offsets": np.array([0, 4])}
     rng = np.random.default_rng(1)
-    for sl in range(1, 29):
-        ids = np.concatenate([np.array([0, -7, V + 5, 3], dtype=np.int64), rng.integers(1, V, 40)])
-        batch[sl] = (ids, np.array([0, 0, 4, 44], dtype=np.int64))
-    vals, offs = _to_dev_batch(torch, batch, dev)
+    for sl in range(1, S + 1):
+        ids = np.concatenate([np.array([0, -7, V + 5, 3], dtype=np.int64), rng.integers(0, V, 43)])
+        batch[sl] = (ids, np.array([0, 0, 4, 44, 47], dtype=np.int64))
+    vals, offs = _to_dev_batch(torch, batch, dev, slots=S)
     q, s, pooled, ln = device_ops.rep_gather_ln_quant(table, vals, offs, g, b, 1e-5, want_pooled=True,
                                                       want_ln=True)
-    oq, os_, opooled, oln = O.rep_forward(table_np, "float32", batch, np.ones(28 * 512, np.float32),
-                                          np.zeros(28 * 512, np.float32), 1e-5, intermediates=True)
-    assert np.array_equal(pooled.cpu().numpy(), opooled)
-    assert np.all(pooled[0].cpu().numpy() == 0)
+    oq, os_, opooled, oln = O.rep_forward(table_np, dt, batch, np.ones(H, np.float32), np.zeros(H, np.float32),
+                                          1e-5, num_slots=S, intermediates=True)
+    assert np.array_equal(_row_f32(torch, pooled), opooled)
+    assert np.all(_row_f32(torch, pooled)[0] == 0)
+    assert np.array_equal(_row_f32(torch, ln), oln)
     assert np.array_equal(q.cpu().numpy(), oq)
     assert np.array_equal(s.cpu().numpy(), os_)
 
