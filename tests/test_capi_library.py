@@ -63,3 +63,54 @@ def test_status_codes_map_to_exceptions():
     rc = lib.rb_rep_gather_ln_quant(None, 1, 10, 256, None, None, None, 28, 5, None, None, 1, 1e-5, 0, None, 0,
                                     None, 14336, None, None, None, None)
     assert rc in (_lib.RB_ERR_VALUE, _lib.RB_ERR_UNSUPPORTED)
+
+
+def test_pool_scatter_rejects_bad_arguments_on_the_host():
+    """rb_rep_gather_pool_scatter validates its destinations before any device
+    work.  The pointers below are never dereferenced: every call fails a host
+    check before the launch (a call that passed them all would launch a kernel on
+    fake addresses, so none may)."""
+    from baidu_cti_grab_b200 import _lib
+
+    lib = _lib.load()
+    S, N, ld = 2, 10, 1024
+    fake = 1 << 20  # 1 MiB: aligned, never dereferenced
+    vals = _lib.ptr_array([fake, fake])
+    offs = _lib.ptr_array([fake, fake])
+    nnz = _lib.i64_array([5, 5])
+    cols = _lib.i32_array([0, 1])
+
+    def call(dest, begin, num_dest, ld=ld, shift=0, cols=cols, nnz=nnz):
+        rc = lib.rb_rep_gather_pool_scatter(fake, _lib.RB_BF16, 100, 512, vals, offs, nnz, cols, S, N,
+                                            _lib.ptr_array(dest), _lib.i64_array(begin), num_dest, ld, shift, None)
+        return rc, _lib.last_error()
+
+    assert call([fake], [0, N], 0)[0] == _lib.RB_ERR_VALUE                       # no destination
+    assert call([fake] * 9, list(range(10)), 9)[0] == _lib.RB_ERR_VALUE          # more than RB_MAX_DEST
+    rc, msg = call([fake, fake], [0, 4, 9], 2)                                   # does not end at num_items
+    assert rc == _lib.RB_ERR_VALUE and "dest_begin" in msg
+    rc, msg = call([fake, fake], [0, 6, 4], 2)                                   # decreasing (and wrong end)
+    assert rc == _lib.RB_ERR_VALUE
+    rc, msg = call([fake + 16, fake], [0, 6, 10], 2)                             # bf16 rows need 32-byte alignment
+    assert rc == _lib.RB_ERR_VALUE and "aligned" in msg
+    rc, msg = call([fake, fake], [0, 6, 10], 2, ld=520)                          # ld breaks the row alignment
+    assert rc == _lib.RB_ERR_VALUE
+    rc, msg = call([fake, fake], [0, 6, 10], 2, cols=_lib.i32_array([0, 2]))    # slot 1 past ld
+    assert rc == _lib.RB_ERR_VALUE and "col_slot" in msg
+    rc, msg = call([fake, fake], [0, 6, 10], 2, shift=N)                         # item_shift out of range
+    assert rc == _lib.RB_ERR_VALUE and "item_shift" in msg
+    rc, msg = call([fake, fake], [0, 6, 10], 2, nnz=_lib.i64_array([5, -1]))    # negative nnz
+    assert rc == _lib.RB_ERR_VALUE
+
+
+def test_ipc_entry_points_reject_null_arguments():
+    import ctypes
+
+    from baidu_cti_grab_b200 import _lib
+
+    lib = _lib.load()
+    off = ctypes.c_int64(0)
+    assert lib.rb_ipc_export(None, None, ctypes.byref(off)) == _lib.RB_ERR_VALUE
+    ptr = ctypes.c_void_p(0)
+    assert lib.rb_ipc_import(None, 0, ctypes.byref(ptr)) == _lib.RB_ERR_VALUE
+    assert lib.rb_ipc_close(None, 0) == _lib.RB_ERR_VALUE
