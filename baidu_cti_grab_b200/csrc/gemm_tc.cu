@@ -25,8 +25,10 @@
 // 256x256 tile on a cluster of two CTAs with tcgen05.mma.cta_group::2; for
 // 17 <= M with fewer tiles than SMs the one-SM kernel splits K across CTAs
 // into an int32 workspace that splitk_finalize_kernel sums in split order; for
-// M <= 16 w8a8_gemv_kernel uses dp4a on the CUDA cores.  No TMA load carries a cluster
-// multicast (only tcgen05.commit signals both CTAs of a pair).  Every mbarrier
+// M <= 16 w8a8_gemv_kernel uses dp4a on the CUDA cores in clusters of 8 CTAs
+// split along K, whose partial sums meet in the leader's shared memory.  No
+// TMA load carries a cluster multicast (only tcgen05.commit signals both CTAs
+// of a pair).  Every mbarrier
 // wait is bounded (common.cuh): on timeout the kernel records a watchdog code,
 // drains what it issued and returns instead of hanging.
 #include <cuda.h>
@@ -704,71 +706,145 @@ __device__ __forceinline__ void epilogue_one(int32_t acc, int64_t m, int64_t n, 
   }
 }
 
-// Small M (M <= kGemvMaxM): reading the [N, K] weight once is the whole cost,
-// and a tensor-core tile would be 1/8 full.  One launch, no workspace: a CTA
-// owns kGemvCols output columns; its threads stride over the 16-byte K chunks,
-// each chunk of B read once (coalesced) and dotted with the same chunk of every
-// row of A through dp4a (exact int32 products and sums); the partial sums meet
-// through warp shuffles and shared memory, then the usual epilogue.  int32
+// Small M (M <= kGemvMaxM): reading the [N, K] weight once is the whole cost
+// (7.3 MB for the RepEncoder's linear), and a tensor-core tile would be 1/8
+// full.  One launch, no workspace.  A cluster of kGvSplit CTAs owns kGvCols
+// output columns; CTA r of the cluster covers the r-th 1/kGvSplit of K.  Warp w
+// owns columns 4w..4w+3 of the cluster and lane l the 16-byte K chunks l,
+// l+32, l+64, l+96 of each round of 128 chunks: a thread issues all sixteen of
+// its weight loads before the first product, so the whole weight is in flight
+// at once (the grid is resident in one wave), and the round's A slice
+// (M x 2 KB) comes into shared memory with cp.async.  Products are exact
+// dp4a; the warp's MT x 4 sums are reduce-scattered over its lanes, written
+// into the leader CTA's shared memory through the cluster's distributed shared
+// memory, and summed there in CTA order before the usual epilogue.  int32
 // addition (modulo 2^32, like the tensor core's) is associative, so the result
 // equals the tiled kernels' bit for bit.
 constexpr int kGemvMaxM = 16;
-constexpr int kGemvCols = 4;
-constexpr int kGemvThreads = 256;
+constexpr int kGvSplit = 8;     // CTAs per cluster, along K
+constexpr int kGvCols = 16;     // output columns per cluster
+constexpr int kGvThreads = 128; // 4 warps x 4 columns
+constexpr int kGvIt = 4;        // chunks per lane per round
+constexpr int kGvRound = 32 * kGvIt;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 template <int MT>
-__global__ void __launch_bounds__(kGemvThreads, 1)
+__global__ void __launch_bounds__(kGvThreads, 3)
     w8a8_gemv_kernel(const int8_t* __restrict__ A, int64_t lda, const int8_t* __restrict__ B, int64_t ldb,
                      const __grid_constant__ EpiParams ep) {
-  __shared__ uint32_t red[kGemvThreads / 32][MT * kGemvCols];
-  const int64_t n0 = (int64_t)blockIdx.x * kGemvCols;
+  constexpr int V = MT * 4;  // sums per warp: rows x 4 columns
+  __shared__ __align__(16) int4 sA[MT][kGvRound];
+  __shared__ __align__(16) uint32_t red[kGvSplit][4][V];
+  // every CTA of the cluster has started before any writes into the leader's
+  // shared memory (the matching wait comes after the products)
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+  const uint32_t rank = pair::cluster_rank();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t n0 = (int64_t)(blockIdx.x / kGvSplit) * kGvCols;
   const int M = (int)ep.M;
   const int64_t chunks = ep.K / 16;
-  int32_t acc[MT][kGemvCols];
+  const int64_t per_cta = (chunks + kGvSplit - 1) / kGvSplit;
+  const int64_t k0 = (int64_t)rank * per_cta;
+  const int64_t k_end = min(chunks, k0 + per_cta);
+  int32_t acc[MT][4];
 #pragma unroll
   for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int c = 0; c < kGemvCols; ++c) acc[m][c] = 0;
-  for (int64_t q = threadIdx.x; q < chunks; q += kGemvThreads) {
-    // every load of the chunk first (one memory round trip), then the dot products
-    int4 b[kGemvCols], a[MT];
+    for (int c = 0; c < 4; ++c) acc[m][c] = 0;
+  for (int64_t r0 = k0; r0 < k_end; r0 += kGvRound) {
+    // A rows of this round into shared memory (zeros past M or the slice)
+    for (int i = threadIdx.x; i < MT * kGvRound; i += kGvThreads) {
+      const int m = i / kGvRound, q = i % kGvRound;
+      const bool ok = m < M && r0 + q < k_end;
+      cp_async16((uint32_t)__cvta_generic_to_shared(&sA[m][q]), ok ? A + m * lda + (r0 + q) * 16 : A, ok ? 16u : 0u);
+    }
+    // every weight load of the round before the first product
+    int4 b[kGvIt][4];
 #pragma unroll
-    for (int c = 0; c < kGemvCols; ++c)
-      b[c] = (n0 + c < ep.N) ? __ldg(reinterpret_cast<const int4*>(B + (n0 + c) * ldb) + q) : make_int4(0, 0, 0, 0);
+    for (int it = 0; it < kGvIt; ++it) {
+      const int64_t q = r0 + lane + 32 * it;
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
-      a[m] = m < M ? __ldg(reinterpret_cast<const int4*>(A + m * lda) + q) : make_int4(0, 0, 0, 0);
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-#pragma unroll
-      for (int c = 0; c < kGemvCols; ++c) {
-        int v = acc[m][c];
-        v = __dp4a(a[m].x, b[c].x, v);
-        v = __dp4a(a[m].y, b[c].y, v);
-        v = __dp4a(a[m].z, b[c].z, v);
-        v = __dp4a(a[m].w, b[c].w, v);
-        acc[m][c] = v;
+      for (int c = 0; c < 4; ++c) {
+        const int64_t n = n0 + 4 * warp + c;
+        b[it][c] = (q < k_end && n < ep.N) ? __ldg(reinterpret_cast<const int4*>(B + n * ldb) + q)
+                                           : make_int4(0, 0, 0, 0);
       }
     }
+    cp_async_wait_all();
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < kGvIt; ++it) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        const int4 a = sA[m][lane + 32 * it];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          int v = acc[m][c];
+          v = __dp4a(a.x, b[it][c].x, v);
+          v = __dp4a(a.y, b[it][c].y, v);
+          v = __dp4a(a.z, b[it][c].z, v);
+          v = __dp4a(a.w, b[it][c].w, v);
+          acc[m][c] = v;
+        }
+      }
+    }
+    __syncthreads();  // sA is rewritten by the next round
   }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // reduce-scatter over the warp: each xor step halves the values a lane
+  // carries until one is left (two when V = 64), then plain xor sums.  Value
+  // j = 4m + c ends on lane j << (5 - log2 V) (and its xor partners) for
+  // V <= 32, and on lane j / 2 for V = 64.
+  uint32_t v[V];
 #pragma unroll
-  for (int m = 0; m < MT; ++m) {
+  for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int c = 0; c < kGemvCols; ++c) {
-      uint32_t v = (uint32_t)acc[m][c];
+    for (int c = 0; c < 4; ++c) v[4 * m + c] = (uint32_t)acc[m][c];
+  int h = V;
 #pragma unroll
-      for (int d = 16; d >= 1; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
-      if (lane == 0) red[warp][m * kGemvCols + c] = v;
+  for (int d = 16; d >= 1; d >>= 1) {
+    if (h > 2 || (h == 2 && V <= 32)) {
+      h >>= 1;
+      const bool upper = (lane & d) != 0;
+#pragma unroll
+      for (int i = 0; i < V / 2; ++i) {
+        if (i < h) {
+          const uint32_t send = upper ? v[i] : v[i + h];
+          const uint32_t keep = upper ? v[i + h] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        if (i < h) v[i] += __shfl_xor_sync(0xffffffffu, v[i], d);
     }
   }
-  __syncthreads();
-  if (threadIdx.x < MT * kGemvCols) {
-    const int m = threadIdx.x / kGemvCols, c = threadIdx.x % kGemvCols;
-    if (m < M && n0 + c < ep.N) {
+  asm volatile("barrier.cluster.wait;" ::: "memory");
+  const uint32_t red_local = (uint32_t)__cvta_generic_to_shared(&red[rank][warp][0]);
+  const uint32_t red_leader = pair::map_rank(red_local, 0);
+  if constexpr (V == 64) {
+    asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(red_leader + 8u * lane), "r"(v[0]), "r"(v[1])
+                 : "memory");
+  } else {
+    constexpr int kShift = 5 - (V == 4 ? 2 : V == 8 ? 3 : V == 16 ? 4 : 5);
+    if ((lane & ((1 << kShift) - 1)) == 0)
+      asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(red_leader + 4u * (lane >> kShift)), "r"(v[0])
+                   : "memory");
+  }
+  pair::cluster_sync_all();
+  if (rank != 0) return;
+  for (int o = threadIdx.x; o < MT * kGvCols; o += kGvThreads) {
+    const int m = o / kGvCols, col = o % kGvCols;
+    const int64_t n = n0 + col;
+    if (m < M && n < ep.N) {
       uint32_t sum = 0;
 #pragma unroll
-      for (int w = 0; w < kGemvThreads / 32; ++w) sum += red[w][threadIdx.x];
-      epilogue_one((int32_t)sum, m, n0 + c, ep);
+      for (int r = 0; r < kGvSplit; ++r) sum += red[r][col >> 2][4 * m + (col & 3)];
+      epilogue_one((int32_t)sum, m, n, ep);
     }
   }
 }
@@ -902,12 +978,25 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
     return check_cuda(cudaGetLastError(), "w8a8_gemm_simple_kernel launch");
   }
   if (M <= kGemvMaxM) {
-    const unsigned grid = (unsigned)((N + kGemvCols - 1) / kGemvCols);
-    if (M <= 1) w8a8_gemv_kernel<1><<<grid, kGemvThreads, 0, st>>>(A, lda, B, ldb, ep);
-    else if (M <= 2) w8a8_gemv_kernel<2><<<grid, kGemvThreads, 0, st>>>(A, lda, B, ldb, ep);
-    else if (M <= 4) w8a8_gemv_kernel<4><<<grid, kGemvThreads, 0, st>>>(A, lda, B, ldb, ep);
-    else if (M <= 8) w8a8_gemv_kernel<8><<<grid, kGemvThreads, 0, st>>>(A, lda, B, ldb, ep);
-    else w8a8_gemv_kernel<16><<<grid, kGemvThreads, 0, st>>>(A, lda, B, ldb, ep);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(((N + kGvCols - 1) / kGvCols) * kGvSplit));
+    cfg.blockDim = dim3(kGvThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kGvSplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t le;
+    if (M <= 1) le = cudaLaunchKernelEx(&cfg, w8a8_gemv_kernel<1>, A, lda, B, ldb, ep);
+    else if (M <= 2) le = cudaLaunchKernelEx(&cfg, w8a8_gemv_kernel<2>, A, lda, B, ldb, ep);
+    else if (M <= 4) le = cudaLaunchKernelEx(&cfg, w8a8_gemv_kernel<4>, A, lda, B, ldb, ep);
+    else if (M <= 8) le = cudaLaunchKernelEx(&cfg, w8a8_gemv_kernel<8>, A, lda, B, ldb, ep);
+    else le = cudaLaunchKernelEx(&cfg, w8a8_gemv_kernel<16>, A, lda, B, ldb, ep);
+    if (le != cudaSuccess) return check_cuda(le, "w8a8_gemv_kernel launch");
     return check_cuda(cudaGetLastError(), "w8a8_gemv_kernel launch");
   }
   int dev = 0;

@@ -50,7 +50,10 @@ def test_gemm_golden(cuda_device):
 @pytest.mark.parametrize("M,K,N", [(1, 14336, 512), (7, 14336, 512), (128, 14336, 512), (129, 4096, 512),
                                    (300, 592, 48), (1000, 14336, 512), (257, 128, 300), (64, 16, 256),
                                    (4096, 14336, 512), (33, 14336, 200), (1024, 14336, 512), (1025, 592, 300),
-                                   (3000, 1024, 48), (2048, 14336, 257)])
+                                   (3000, 1024, 48), (2048, 14336, 257),
+                                   # M <= 16: one 16-byte K chunk, K over one round of
+                                   # 128 chunks per CTA, column counts off the 16-column groups
+                                   (3, 16, 48), (16, 16400, 40), (9, 2064, 17), (2, 14336, 1)])
 def test_gemm_random_shapes(cuda_device, M, K, N):
     import torch
     from oracle import oracle as O
