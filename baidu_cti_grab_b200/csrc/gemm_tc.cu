@@ -750,6 +750,22 @@ __global__ void __launch_bounds__(kGvThreads, 3)
   const int64_t per_cta = (chunks + kGvSplit - 1) / kGvSplit;
   const int64_t k0 = (int64_t)rank * per_cta;
   const int64_t k_end = min(chunks, k0 + per_cta);
+  // the leader's epilogue operands, requested now so that their latency
+  // overlaps the loads and products instead of following the last barrier
+  constexpr int kPer = (MT * kGvCols + kGvThreads - 1) / kGvThreads;
+  float e_sa[kPer], e_sb[kPer], e_bi[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    e_sa[j] = e_sb[j] = e_bi[j] = 0.0f;
+    const int o = threadIdx.x + j * kGvThreads;
+    const int m = o / kGvCols;
+    const int64_t n = n0 + o % kGvCols;
+    if (rank == 0 && ep.out_dtype != RB_I32 && o < MT * kGvCols && m < M && n < ep.N) {
+      e_sa[j] = load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? m : 0);
+      e_sb[j] = load_as_f32(ep.sb, ep.sb_dtype, n);
+      if (ep.bias != nullptr) e_bi[j] = load_as_f32(ep.bias, ep.bias_dtype, n);
+    }
+  }
   int32_t acc[MT][4];
 #pragma unroll
   for (int m = 0; m < MT; ++m)
@@ -837,14 +853,29 @@ __global__ void __launch_bounds__(kGvThreads, 3)
   }
   pair::cluster_sync_all();
   if (rank != 0) return;
-  for (int o = threadIdx.x; o < MT * kGvCols; o += kGvThreads) {
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int o = threadIdx.x + j * kGvThreads;
     const int m = o / kGvCols, col = o % kGvCols;
     const int64_t n = n0 + col;
-    if (m < M && n < ep.N) {
+    if (o < MT * kGvCols && m < M && n < ep.N) {
       uint32_t sum = 0;
 #pragma unroll
       for (int r = 0; r < kGvSplit; ++r) sum += red[r][col >> 2][4 * m + (col & 3)];
-      epilogue_one((int32_t)sum, m, n, ep);
+      if (ep.out_dtype == RB_I32) {
+        reinterpret_cast<int32_t*>(ep.out)[m * ep.ldo + n] = (int32_t)sum;
+        continue;
+      }
+      // the epilogue_one arithmetic on the preloaded operands
+      float v = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)sum), e_sa[j]), e_sb[j]);
+      if (ep.bias != nullptr) v = __fadd_rn(v, e_bi[j]);
+      if (ep.out_dtype == RB_F32) {
+        reinterpret_cast<float*>(ep.out)[m * ep.ldo + n] = v;
+      } else if (ep.out_dtype == RB_BF16) {
+        reinterpret_cast<__nv_bfloat16*>(ep.out)[m * ep.ldo + n] = __float2bfloat16_rn(v);
+      } else {
+        reinterpret_cast<__half*>(ep.out)[m * ep.ldo + n] = __float2half_rn(v);
+      }
     }
   }
 }
@@ -916,14 +947,18 @@ static std::once_flag g_pair_attr_once[64];
 using namespace rb;
 
 // split-K factor for the one-SM kernel (1 = no split): enough (m, n, k) tiles to
-// cover the SMs, at least two K blocks per split
+// cover the SMs, at least two K blocks per split, and at most kMaxKSplits: every
+// split writes and the finalize reads back an M x N int32 partial, which past
+// 16 splits costs more than the extra SMs gain (K = 14336, N = 512 on a B200:
+// 17.6 -> 15.0 us at M = 256, 12.5 -> 11.8 us at M = 64, M = 17 unchanged).
+constexpr int64_t kMaxKSplits = 16;
 static int choose_ksplits(int64_t M, int64_t N, int64_t K) {
   using namespace rb::tc;
   if (M >= RB_GEMM_PAIR_MIN_M || M <= tc::kGemvMaxM || K <= 0 || K % 16 != 0) return 1;
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int64_t kblocks = (K + BK - 1) / BK;
   int64_t s = std::min<int64_t>(sm_count() / std::max<int64_t>(tiles, 1), kblocks / 2);
-  return (int)std::max<int64_t>(1, std::min<int64_t>(s, 256));
+  return (int)std::max<int64_t>(1, std::min<int64_t>(s, kMaxKSplits));
 }
 
 extern "C" int64_t rb_w8a8_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
