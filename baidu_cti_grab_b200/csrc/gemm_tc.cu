@@ -39,11 +39,14 @@
 
 #include "common.cuh"
 
-// smallest M that uses the two-SM kernel: 256-row pair tiles must fill about
-// two waves of the 74 CTA pairs; below it the one-SM kernel, split along K,
-// spreads the work over all SMs
+// smallest M that uses the two-SM kernel.  Per SM a pair tile loads a third
+// fewer operand bytes per MMA than a one-SM tile, and from M = 4096 (16 row
+// blocks of 256, 32 pairs) that outweighs the idle SMs: at K = 14336, N = 512
+// on a B200 it takes 57 / 57 / 59 / 90 us at M = 4096 / 6144 / 8192 / 12288
+// against 58 / 64 / 66 / 103 us for the split one-SM kernel.  Below it the
+// one-SM kernel, split along K, spreads the work over all SMs.
 #ifndef RB_GEMM_PAIR_MIN_M
-#define RB_GEMM_PAIR_MIN_M 16384
+#define RB_GEMM_PAIR_MIN_M 4096
 #endif
 
 namespace rb {

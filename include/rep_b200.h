@@ -188,7 +188,7 @@ int rb_pack_weight_nk(const int8_t* src, int64_t K, int64_t N, int64_t stride_k,
  * Replaces quantization/w8a8_triton_kernels.py:174-318,470-640
  * (w8a8_scaled_mm[_out], int8_mm_no_scale[_out]) and kernels/quantization.py:38-105
  * (_w8a8_matmul_kernel).  tcgen05 kind::i8 on sm_100a with the accumulator in TMEM
- * (one-SM tiles; CTA-pair tiles for M >= 16384); M <= 16 uses int8 dot products
+ * (one-SM tiles; CTA-pair tiles for M >= 4096); M <= 16 uses int8 dot products
  * on the CUDA cores (one launch), with the same results bit for bit.
  *   A     int8 [M, lda]  (K contiguous; lda % 16 == 0, 16-byte aligned)
  *   B     int8 [N, ldb]  (K contiguous; ldb % 16 == 0, 16-byte aligned)
