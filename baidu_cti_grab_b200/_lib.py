@@ -18,7 +18,7 @@ from typing import Optional
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "librep_b200.so")
 
-RB_F32, RB_BF16, RB_F16, RB_I32, RB_I8 = 0, 1, 2, 3, 4
+RB_F32, RB_BF16, RB_F16, RB_I32, RB_I8, RB_I64 = 0, 1, 2, 3, 4, 5
 RB_ACT_DYNAMIC, RB_ACT_STATIC, RB_ACT_NONE = 0, 1, 2
 RB_OK, RB_ERR_VALUE, RB_ERR_UNSUPPORTED, RB_ERR_CUDA, RB_ERR_DEVICE = 0, 1, 2, 3, 4
 RB_MAX_SLOTS = 32
@@ -32,6 +32,8 @@ _pp = ctypes.POINTER(ctypes.c_void_p)
 SIGNATURES = {
     "rb_rep_gather_ln_quant": [_vp, _i32, _i64, _i32, _vp, _vp, _vp, _i32, _i64, _vp, _vp, _i32, _f32,
                                _i32, _vp, _i32, _vp, _i64, _vp, _vp, _vp, _vp],
+    "rb_rep_gather_ln_quant_idx": [_vp, _i32, _i64, _i32, _i32, _vp, _vp, _vp, _i32, _i64, _vp, _vp, _i32, _f32,
+                                   _i32, _vp, _i32, _vp, _i64, _vp, _vp, _vp, _vp],
     "rb_rep_gather_pool": [_vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64, _vp],
     "rb_layernorm_quant": [_vp, _i32, _i64, _i32, _i64, _vp, _vp, _i32, _f32, _i32, _vp, _i32, _vp, _i64,
                            _vp, _vp, _vp],

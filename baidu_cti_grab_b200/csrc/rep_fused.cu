@@ -16,7 +16,8 @@
 // round-to-nearest operation so the result is reproducible bit for bit.
 //
 // HBM traffic per item (bf16 table, k ids per slot): 28*k*1 KB of table rows
-// + 28*k*8 B ids + 28*2*8 B offsets + 14336 B int8 + 4 B scale.
+// + 28*k*8 B ids + 28*2*8 B offsets (4 B each with int32 indices) + 14336 B
+// int8 + 4 B scale.
 #include "common.cuh"
 
 namespace rb {
@@ -30,8 +31,10 @@ constexpr int kDim = 512;
 enum RepMode : int { kGatherLnQuant = 0, kGatherPool = 1, kDenseLnQuant = 2 };
 
 struct SlotArgs {
-  const int64_t* values[RB_MAX_SLOTS];
-  const int64_t* offsets[RB_MAX_SLOTS];
+  // ids and offsets of each slot: int64, or int32 for the kernels instantiated
+  // with IdxT = int32_t (the kernel reads them through IdxT)
+  const void* values[RB_MAX_SLOTS];
+  const void* offsets[RB_MAX_SLOTS];
   int64_t nnz[RB_MAX_SLOTS];
   int col_slot[RB_MAX_SLOTS];
 };
@@ -295,7 +298,7 @@ __device__ __forceinline__ V sel4(const V* a, int j) {
 // thread) keeps five 7-warp CTAs resident per SM: the gather's latency needs
 // that occupancy more than the code needs registers.  An fp32 row takes 56 KB
 // of shared memory, so at most three CTAs fit and the budget is larger.
-template <typename T, int MODE, int kS, typename TA>
+template <typename T, int MODE, int kS, typename TA, typename IdxT>
 __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(const __grid_constant__ RepParams p) {
   constexpr bool kBf16 = sizeof(T) == 2;
   constexpr int kRows = kBf16 ? RB_K1_BF16_ROWS : 2;  // table rows a warp holds in registers
@@ -437,8 +440,8 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       if (lane < 8 && j < nsl) {
         const int s = slot_of(j);
         const int64_t nz = p.slots.nnz[s];
-        const int64_t* off = p.slots.offsets[s];
-        const int64_t b = (lane < 4) ? off[item] : ((item + 1 < p.num_items) ? off[item + 1] : nz);
+        const IdxT* off = static_cast<const IdxT*>(p.slots.offsets[s]);
+        const int64_t b = (lane < 4) ? (int64_t)off[item] : ((item + 1 < p.num_items) ? (int64_t)off[item + 1] : nz);
         bound = b < 0 ? 0 : (b > nz ? nz : b);
       }
     }
@@ -463,7 +466,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       int id = 0;
       if (t < total) {
         const int j = (t >= pre[1]) + (t >= pre[2]) + (t >= pre[3]);
-        const int64_t v = p.slots.values[slot_of(j)][sel4(start, j) + (t - sel4(pre, j))];
+        const int64_t v = static_cast<const IdxT*>(p.slots.values[slot_of(j)])[sel4(start, j) + (t - sel4(pre, j))];
         id = (int)(v < 0 ? 0 : (v > vmax ? vmax : v));
         if (id != 0) prefetch_l2_bulk(table + (int64_t)id * kDim, kDim * (int)sizeof(T));
       }
@@ -676,7 +679,7 @@ static int validate_common(int num_slots, int64_t num_items) {
   return RB_OK;
 }
 
-static int fill_slots(SlotArgs& sa, const int64_t* const* values, const int64_t* const* offsets,
+static int fill_slots(SlotArgs& sa, const void* const* values, const void* const* offsets,
                       const int64_t* nnz, const int* col_slot, int num_slots, int64_t num_items) {
   for (int s = 0; s < num_slots; ++s) {
     if (offsets == nullptr || offsets[s] == nullptr)
@@ -693,7 +696,7 @@ static int fill_slots(SlotArgs& sa, const int64_t* const* values, const int64_t*
   return RB_OK;
 }
 
-template <int MODE>
+template <int MODE, typename IdxT = int64_t>
 static int launch_rep(const RepParams& p, int row_dtype, cudaStream_t stream) {
   if (p.num_items == 0) return RB_OK;
   const int warps = (p.num_slots + kSlotsPerWarp - 1) / kSlotsPerWarp;
@@ -705,13 +708,16 @@ static int launch_rep(const RepParams& p, int row_dtype, cudaStream_t stream) {
   const bool s28 = p.num_slots == 28;
   // gamma/beta storage: 16-bit words or fp32 (the pooling-only mode reads neither)
   const bool a16 = MODE != kGatherPool && p.ln_dtype != RB_F32;
+  using B16 = __nv_bfloat16;
   auto kern = row_dtype == RB_BF16
-                  ? (s28 ? (a16 ? rep_fused_kernel<__nv_bfloat16, MODE, 28, uint16_t>
-                                : rep_fused_kernel<__nv_bfloat16, MODE, 28, float>)
-                         : (a16 ? rep_fused_kernel<__nv_bfloat16, MODE, 0, uint16_t>
-                                : rep_fused_kernel<__nv_bfloat16, MODE, 0, float>))
-                  : (s28 ? (a16 ? rep_fused_kernel<float, MODE, 28, uint16_t> : rep_fused_kernel<float, MODE, 28, float>)
-                         : (a16 ? rep_fused_kernel<float, MODE, 0, uint16_t> : rep_fused_kernel<float, MODE, 0, float>));
+                  ? (s28 ? (a16 ? rep_fused_kernel<B16, MODE, 28, uint16_t, IdxT>
+                                : rep_fused_kernel<B16, MODE, 28, float, IdxT>)
+                         : (a16 ? rep_fused_kernel<B16, MODE, 0, uint16_t, IdxT>
+                                : rep_fused_kernel<B16, MODE, 0, float, IdxT>))
+                  : (s28 ? (a16 ? rep_fused_kernel<float, MODE, 28, uint16_t, IdxT>
+                                : rep_fused_kernel<float, MODE, 28, float, IdxT>)
+                         : (a16 ? rep_fused_kernel<float, MODE, 0, uint16_t, IdxT>
+                                : rep_fused_kernel<float, MODE, 0, float, IdxT>));
   if (smem > 48 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess) kern<<<grid, block, smem, stream>>>(p);
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(rep_fused_kernel)");
@@ -749,13 +755,14 @@ static int check_ln_args(const void* gamma, const void* beta, int ln_dtype, int 
 
 using namespace rb;
 
-extern "C" int rb_rep_gather_ln_quant(const void* table, int table_dtype, int64_t num_rows, int emb_dim,
-                                      const int64_t* const* slot_values, const int64_t* const* slot_offsets,
-                                      const int64_t* slot_nnz, int num_slots, int64_t num_items,
-                                      const void* ln_gamma, const void* ln_beta, int ln_dtype, float eps,
-                                      int act_mode, const void* static_scale, int static_scale_dtype,
-                                      int8_t* q_out, int64_t ldq, float* scale_out, void* pooled_out,
-                                      void* ln_out, void* stream) {
+static int gather_ln_quant(const void* table, int table_dtype, int64_t num_rows, int emb_dim, int index_dtype,
+                           const void* const* slot_values, const void* const* slot_offsets,
+                           const int64_t* slot_nnz, int num_slots, int64_t num_items, const void* ln_gamma,
+                           const void* ln_beta, int ln_dtype, float eps, int act_mode, const void* static_scale,
+                           int static_scale_dtype, int8_t* q_out, int64_t ldq, float* scale_out, void* pooled_out,
+                           void* ln_out, void* stream) {
+  if (index_dtype != RB_I64 && index_dtype != RB_I32)
+    return fail(RB_ERR_VALUE, "index dtype must be RB_I64 or RB_I32, got %d", index_dtype);
   int rc = validate_common(num_slots, num_items);
   if (rc) return rc;
   if (emb_dim != kDim) return fail(RB_ERR_UNSUPPORTED, "emb_dim must be 512, got %d", emb_dim);
@@ -791,7 +798,35 @@ extern "C" int rb_rep_gather_ln_quant(const void* table, int table_dtype, int64_
   p.pooled = pooled_out;
   p.ldp = (int64_t)num_slots * kDim;
   p.ln = ln_out;
-  return launch_rep<kGatherLnQuant>(p, table_dtype, (cudaStream_t)stream);
+  return index_dtype == RB_I32 ? launch_rep<kGatherLnQuant, int32_t>(p, table_dtype, (cudaStream_t)stream)
+                               : launch_rep<kGatherLnQuant, int64_t>(p, table_dtype, (cudaStream_t)stream);
+}
+
+extern "C" int rb_rep_gather_ln_quant(const void* table, int table_dtype, int64_t num_rows, int emb_dim,
+                                      const int64_t* const* slot_values, const int64_t* const* slot_offsets,
+                                      const int64_t* slot_nnz, int num_slots, int64_t num_items,
+                                      const void* ln_gamma, const void* ln_beta, int ln_dtype, float eps,
+                                      int act_mode, const void* static_scale, int static_scale_dtype,
+                                      int8_t* q_out, int64_t ldq, float* scale_out, void* pooled_out,
+                                      void* ln_out, void* stream) {
+  return gather_ln_quant(table, table_dtype, num_rows, emb_dim, RB_I64,
+                         reinterpret_cast<const void* const*>(slot_values),
+                         reinterpret_cast<const void* const*>(slot_offsets), slot_nnz, num_slots, num_items,
+                         ln_gamma, ln_beta, ln_dtype, eps, act_mode, static_scale, static_scale_dtype, q_out, ldq,
+                         scale_out, pooled_out, ln_out, stream);
+}
+
+extern "C" int rb_rep_gather_ln_quant_idx(const void* table, int table_dtype, int64_t num_rows, int emb_dim,
+                                          int index_dtype, const void* const* slot_values,
+                                          const void* const* slot_offsets, const int64_t* slot_nnz,
+                                          int num_slots, int64_t num_items, const void* ln_gamma,
+                                          const void* ln_beta, int ln_dtype, float eps, int act_mode,
+                                          const void* static_scale, int static_scale_dtype, int8_t* q_out,
+                                          int64_t ldq, float* scale_out, void* pooled_out, void* ln_out,
+                                          void* stream) {
+  return gather_ln_quant(table, table_dtype, num_rows, emb_dim, index_dtype, slot_values, slot_offsets, slot_nnz,
+                         num_slots, num_items, ln_gamma, ln_beta, ln_dtype, eps, act_mode, static_scale,
+                         static_scale_dtype, q_out, ldq, scale_out, pooled_out, ln_out, stream);
 }
 
 extern "C" int rb_rep_gather_pool(const void* table, int table_dtype, int64_t num_rows, int emb_dim,
@@ -815,7 +850,8 @@ extern "C" int rb_rep_gather_pool(const void* table, int table_dtype, int64_t nu
     if (col_slot[s] < 0 || (int64_t)(col_slot[s] + 1) * kDim > ldp)
       return fail(RB_ERR_VALUE, "col_slot[%d]=%d does not fit in ldp=%lld", s, col_slot[s], (long long)ldp);
   RepParams p{};
-  rc = fill_slots(p.slots, slot_values, slot_offsets, slot_nnz, col_slot, num_slots, num_items);
+  rc = fill_slots(p.slots, reinterpret_cast<const void* const*>(slot_values),
+                  reinterpret_cast<const void* const*>(slot_offsets), slot_nnz, col_slot, num_slots, num_items);
   if (rc) return rc;
   p.table = table;
   p.num_rows = num_rows;
@@ -859,7 +895,8 @@ extern "C" int rb_rep_gather_pool_scatter(const void* table, int table_dtype, in
   if (num_items == 0) return RB_OK;
   if (item_shift < 0 || item_shift >= num_items) return fail(RB_ERR_VALUE, "item_shift must be in [0, num_items)");
   RepParams p{};
-  rc = fill_slots(p.slots, slot_values, slot_offsets, slot_nnz, col_slot, num_slots, num_items);
+  rc = fill_slots(p.slots, reinterpret_cast<const void* const*>(slot_values),
+                  reinterpret_cast<const void* const*>(slot_offsets), slot_nnz, col_slot, num_slots, num_items);
   if (rc) return rc;
   p.table = table;
   p.num_rows = num_rows;

@@ -95,8 +95,10 @@ def rep_gather_ln_quant(table: torch.Tensor, slot_values: Sequence[torch.Tensor]
                         eps: float, act_mode: str = "dynamic", static_scale: Optional[torch.Tensor] = None,
                         q_out: Optional[torch.Tensor] = None, scale_out: Optional[torch.Tensor] = None,
                         want_pooled: bool = False, want_ln: bool = False):
-    """Fused gather -> pool -> concat -> LayerNorm -> int8 (rb_rep_gather_ln_quant).
+    """Fused gather -> pool -> concat -> LayerNorm -> int8 (rb_rep_gather_ln_quant_idx).
 
+    Slot values and offsets are all int64 (the reference's collate output) or all
+    int32 (half the bytes; ids, offsets and nnz below 2^31).
     Returns (q int8[N, S*512] or None, scale fp32[N] or None, pooled or None, ln or None)."""
     S = len(slot_values)
     dev = require_cuda("rep_gather_ln_quant", table, gamma, beta, *slot_values, *slot_offsets)
@@ -105,9 +107,12 @@ def rep_gather_ln_quant(table: torch.Tensor, slot_values: Sequence[torch.Tensor]
     if table.dim() != 2 or not table.is_contiguous():
         raise ValueError("table must be a contiguous [V, 512] tensor")
     n_items = int(slot_offsets[0].numel()) - 1 if S else 0
+    idx_dtype = slot_offsets[0].dtype if S else torch.int64
+    if idx_dtype not in (torch.int64, torch.int32):
+        raise ValueError("slot values and offsets must be int64 or int32")
     for s in range(S):
-        if slot_values[s].dtype != torch.int64 or slot_offsets[s].dtype != torch.int64:
-            raise ValueError("slot values and offsets must be int64")
+        if slot_values[s].dtype != idx_dtype or slot_offsets[s].dtype != idx_dtype:
+            raise ValueError("slot values and offsets must all be int64 or all int32")
         if not slot_values[s].is_contiguous() or not slot_offsets[s].is_contiguous():
             raise ValueError("slot values and offsets must be contiguous")
         if slot_offsets[s].numel() - 1 != n_items:
@@ -126,7 +131,8 @@ def rep_gather_ln_quant(table: torch.Tensor, slot_values: Sequence[torch.Tensor]
     if static_scale is not None:
         static_scale = static_scale.contiguous()
     with torch.cuda.device(dev):
-        L.call("rb_rep_gather_ln_quant", table.data_ptr(), rb_dtype(table), table.shape[0], table.shape[1],
+        L.call("rb_rep_gather_ln_quant_idx", table.data_ptr(), rb_dtype(table), table.shape[0], table.shape[1],
+               L.RB_I32 if idx_dtype == torch.int32 else L.RB_I64,
                L.ptr_array([v.data_ptr() for v in slot_values]),
                L.ptr_array([o.data_ptr() for o in slot_offsets]),
                L.i64_array([v.numel() for v in slot_values]), S, n_items,

@@ -2,9 +2,11 @@
 
 A serving loop hands the model one batch dict after another from host
 memory.  ``pack_batch`` packs a batch's 28 (values, offsets) pairs into one
-pinned int64 buffer, cut into item chunks: each chunk holds its own items'
-values and offsets (rebased to the chunk), so one contiguous copy brings a
-chunk to the device.  ``HostPipeline`` then runs, on three CUDA streams,
+pinned buffer, cut into item chunks: each chunk holds its own items' values
+and offsets (rebased to the chunk), so one contiguous copy brings a chunk to
+the device.  The buffer is int32 when every id and offset fits (half the bytes
+of the reference's int64 collate output; the kernel widens them, so results
+are identical), else int64.  ``HostPipeline`` then runs, on three CUDA streams,
 
     copy-in (H2D of chunk c+1) | compute (K1 + K2 of chunk c) | copy-out (D2H of chunk c-1)
 
@@ -36,7 +38,7 @@ DEFAULT_CHUNK_ITEMS = 65536
 class PackedChunk:
     """Items [item_begin, item_begin + num_items) of a packed batch."""
 
-    start: int          # first int64 element of the chunk in the packed buffer
+    start: int          # first element of the chunk in the packed buffer
     lengths: List[int]  # values of slots 1..S, then offsets of slots 1..S (rebased to the chunk)
     item_begin: int
     num_items: int
@@ -48,17 +50,17 @@ class PackedChunk:
 
 @dataclass
 class PackedBatch:
-    """One batch in a single pinned int64 buffer, chunk after chunk; a chunk
+    """One batch in a single pinned int32/int64 buffer, chunk after chunk; a chunk
     holds the values of slots 1..S, then their offsets rebased to the chunk."""
 
-    host: torch.Tensor  # pinned int64
+    host: torch.Tensor  # pinned int32 or int64
     chunks: List[PackedChunk]
     num_slots: int
     num_items: int
 
     @property
     def nbytes(self) -> int:
-        return self.host.numel() * 8
+        return self.host.numel() * self.host.element_size()
 
     @property
     def num_ids(self) -> int:
@@ -70,8 +72,11 @@ def _as_np(a) -> np.ndarray:
 
 
 def pack_batch(batch: Dict[object, object], num_slots: int = 28, pin: bool = True,
-               chunk_items: Optional[int] = DEFAULT_CHUNK_ITEMS) -> PackedBatch:
+               chunk_items: Optional[int] = DEFAULT_CHUNK_ITEMS, index_dtype: str = "auto") -> PackedBatch:
     """Pack a reference batch dict (numpy arrays or CPU tensors) into one pinned buffer.
+
+    ``index_dtype``: "int64", "int32" (ValueError if an id or offset does not
+    fit) or "auto" (int32 when everything fits, else int64).
 
     With ``chunk_items`` (None: one chunk) the items are cut into about equal
     chunks of at most that many.  Every chunk computes exactly what the whole
@@ -109,7 +114,16 @@ def pack_batch(batch: Dict[object, object], num_slots: int = 28, pin: bool = Tru
             parts.append(p)
         chunks.append(PackedChunk(pos, lengths, i0, i1 - i0))
         pos += sum(lengths)
-    host = torch.from_numpy(np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64))
+    flat = np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64)
+    if index_dtype not in ("auto", "int32", "int64"):
+        raise ValueError("index_dtype must be 'auto', 'int32' or 'int64'")
+    if index_dtype != "int64":
+        fits = flat.size == 0 or (int(flat.min()) >= -(1 << 31) and int(flat.max()) < (1 << 31))
+        if fits:
+            flat = flat.astype(np.int32)
+        elif index_dtype == "int32":
+            raise ValueError("an id or offset does not fit in int32; pack with index_dtype='int64'")
+    host = torch.from_numpy(flat)
     if pin:
         host = host.pin_memory()
     return PackedBatch(host, chunks, num_slots, n)
@@ -138,7 +152,8 @@ class HostPipeline:
         self.s_comp = torch.cuda.Stream(dev)
         self.s_out = torch.cuda.Stream(dev)
         S = rep.slot_num
-        self.in_bufs = [torch.empty(max_ids + S * (max_items + max_chunks), dtype=torch.int64, device=dev)
+        # raw bytes, viewed as each batch's index type (int32 or int64)
+        self.in_bufs = [torch.empty(8 * (max_ids + S * (max_items + max_chunks)), dtype=torch.uint8, device=dev)
                         for _ in range(depth)]
         d_model = rep.linear.weight.shape[0] if hasattr(rep.linear, "weight") else rep.linear.qweight_t.shape[1]
         self.out_bufs = [torch.empty((max_items, d_model), dtype=rep.emb.weight.dtype, device=dev)
@@ -162,7 +177,7 @@ class HostPipeline:
         Returns after the work is enqueued; synchronise the device (or ``self.s_out``) to wait."""
         for i, pb in enumerate(batches):
             k = i % self.depth
-            inb, outb = self.in_bufs[k], self.out_bufs[k]
+            inb, outb = self.in_bufs[k].view(pb.host.dtype), self.out_bufs[k]
             if pb.host.numel() > inb.numel() or pb.num_items > outb.shape[0]:
                 raise ValueError("batch larger than the pipeline's max_ids / max_items / max_chunks")
             self.s_in.wait_event(self.in_free[k])

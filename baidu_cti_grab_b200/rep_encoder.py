@@ -35,6 +35,9 @@ FUSE_MODE = "b200"
 
 
 def _slot_tensors(batch, slot_num: int, device: torch.device):
+    """Device values/offsets of every slot: int32 when the batch holds only int32
+    arrays (the packed ingestion format, half the bytes), else int64 as in the
+    reference's collate."""
     values, offsets = [], []
     for i in range(slot_num):
         v, o = batch[i + 1]
@@ -44,14 +47,11 @@ def _slot_tensors(batch, slot_num: int, device: torch.device):
             o = torch.as_tensor(o)
         if v.device != device:
             v = v.to(device, non_blocking=True)
-        o = o.to(v.device)  # models.py:31
-        if v.dtype != torch.int64:
-            v = v.long()
-        if o.dtype != torch.int64:
-            o = o.long()
-        values.append(v.contiguous())
-        offsets.append(o.contiguous())
-    return values, offsets
+        values.append(v)
+        offsets.append(o.to(v.device))  # models.py:31
+    all32 = all(t.dtype == torch.int32 for t in values + offsets)
+    idx = torch.int32 if all32 else torch.int64
+    return ([v.to(idx).contiguous() for v in values], [o.to(idx).contiguous() for o in offsets])
 
 
 def _quantized_weight(rep: nn.Module):

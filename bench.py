@@ -460,7 +460,7 @@ def b200_arm(args):
         e_ms = e0.elapsed_time(e1)
         e_items = sum(pb.num_items for pb in seq)
         e2e = [e_items, e_ms, sum(pb.nbytes for pb in seq) / K, sum(pb.num_items * D_OUT * 2 for pb in seq) / K,
-               chunk_items]
+               chunk_items, str(seq[0].host.dtype).replace("torch.", "")]
 
     # ---- max over ranks
     vals = torch.tensor([ms, e2e[1] if e2e else 0.0, k1_ms, k2_ms], dtype=torch.float64, device=dev)
@@ -527,10 +527,11 @@ def b200_arm(args):
         if e2e is not None:
             line["e2e"] = {"value": round(e2e_items_all / (e2e_ms_max * 1e-3), 1), "unit": "items/s",
                            "h2d_bytes_per_step": int(e2e[2]), "d2h_bytes_per_step": int(e2e[3]),
-                           "chunk_items": e2e[4],
+                           "chunk_items": e2e[4], "index_dtype": e2e[5],
                            "api": "HostPipeline.run -> rep_encoder_forward (fuse_mode b200): per chunk of a batch's "
-                                  "items one pinned H2D copy of its packed ids/offsets, K1 + K2, and one D2H copy "
-                                  "of its bf16 output rows; copies of one chunk overlap the kernels of the next"}
+                                  "items one pinned H2D copy of its packed ids/offsets (int32 when they fit), "
+                                  "K1 + K2, and one D2H copy of its bf16 output rows; copies of one chunk overlap "
+                                  "the kernels of the next"}
 
     # ---- CPU baseline (rank 0, N=1 only)
     if world > 1:

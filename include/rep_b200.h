@@ -20,7 +20,7 @@ extern "C" {
 #endif
 
 /* element types */
-enum rb_dtype { RB_F32 = 0, RB_BF16 = 1, RB_F16 = 2, RB_I32 = 3, RB_I8 = 4 };
+enum rb_dtype { RB_F32 = 0, RB_BF16 = 1, RB_F16 = 2, RB_I32 = 3, RB_I8 = 4, RB_I64 = 5 };
 
 /* activation quantisation: dynamic per-token, static per-tensor, or none (LayerNorm output only) */
 enum rb_act_mode { RB_ACT_DYNAMIC = 0, RB_ACT_STATIC = 1, RB_ACT_NONE = 2 };
@@ -85,6 +85,22 @@ int rb_rep_gather_ln_quant(const void* table, int table_dtype, int64_t num_rows,
                            int act_mode, const void* static_scale, int static_scale_dtype,
                            int8_t* q_out, int64_t ldq, float* scale_out, void* pooled_out,
                            void* ln_out, void* stream);
+
+/*
+ * rb_rep_gather_ln_quant with the width of the ids and offsets as a parameter:
+ * index_dtype RB_I64 (the reference's collate output, models.py:27-34 reads
+ * int64 `values`/`offsets`) or RB_I32 (half the bytes to pack, copy and read;
+ * valid while ids, offsets and nnz stay below 2^31, e.g. a table of fewer than
+ * 2^31 rows).  slot_values[s] / slot_offsets[s] point to arrays of that type;
+ * everything else, the arithmetic included, is as in rb_rep_gather_ln_quant.
+ */
+int rb_rep_gather_ln_quant_idx(const void* table, int table_dtype, int64_t num_rows, int emb_dim,
+                               int index_dtype, const void* const* slot_values, const void* const* slot_offsets,
+                               const int64_t* slot_nnz, int num_slots, int64_t num_items,
+                               const void* ln_gamma, const void* ln_beta, int ln_dtype, float eps,
+                               int act_mode, const void* static_scale, int static_scale_dtype,
+                               int8_t* q_out, int64_t ldq, float* scale_out, void* pooled_out,
+                               void* ln_out, void* stream);
 
 /*
  * Gather + sum-pool only (models.py:27-34, the 28 nn.EmbeddingBag calls), for

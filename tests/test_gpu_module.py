@@ -173,10 +173,12 @@ def test_static_quantised_checkpoint_layer(cuda_device):
     assert torch.equal(out, ref)
 
 
+@pytest.mark.parametrize("index_dtype", ["auto", "int64"])
 @pytest.mark.parametrize("chunk_items", [None, 700, 97])
-def test_host_pipeline_matches_direct_forward(cuda_device, chunk_items):
+def test_host_pipeline_matches_direct_forward(cuda_device, chunk_items, index_dtype):
     """HostPipeline (overlapped H2D / forward / D2H), with whole batches and
-    with batches cut into item chunks, returns exactly the direct forward's output."""
+    with batches cut into item chunks, packed as int32 (auto) or int64, returns
+    exactly the direct forward's output on the reference's int64 batch."""
     import torch
     from baidu_cti_grab_b200 import synth
     from baidu_cti_grab_b200.pipeline import HostPipeline, pack_batch
@@ -185,7 +187,9 @@ def test_host_pipeline_matches_direct_forward(cuda_device, chunk_items):
     rep, _, _ = _setup(torch, cuda_device, users=4, seed=26)
     cfg = synth.WorkloadConfig("pipe", 2000, "bfloat16", 40, 1, 90, "1+poisson1", 1.1)
     host = [synth.make_batch(cfg, seed=100 + i) for i in range(5)]
-    packed = [pack_batch(b, chunk_items=chunk_items) for b in host]
+    packed = [pack_batch(b, chunk_items=chunk_items, index_dtype=index_dtype) for b in host]
+    want = torch.int32 if index_dtype == "auto" else torch.int64
+    assert all(pb.host.dtype == want for pb in packed)
     if chunk_items == 97:
         assert all(len(pb.chunks) > 10 for pb in packed)
     outs = [torch.empty((pb.num_items, 512), dtype=torch.bfloat16).pin_memory() for pb in packed]

@@ -183,6 +183,45 @@ def test_k1_edge_cases(cuda_device, dt, S):
     assert np.array_equal(s.cpu().numpy(), os_)
 
 
+@pytest.mark.parametrize("dt,S", [("bfloat16", 28), ("float32", 28), ("bfloat16", 5)])
+def test_k1_int32_indices_equal_int64(cuda_device, dt, S):
+    """Ids and offsets given as int32 (the packed ingestion format) give the same
+    bits as int64 in every output: pooled rows, LayerNorm rows, int8 and scales,
+    on a synthetic batch and on padding / negative / out-of-range ids, an empty
+    bag, a 40-id bag and an odd-length bag.  Mixed widths are refused."""
+    import torch
+    from oracle import oracle as O
+    from baidu_cti_grab_b200 import device_ops, synth
+
+    dev = cuda_device
+    V = 300
+    H = S * 512
+    t32 = (np.random.default_rng(5).standard_normal((V, 512)) * 0.02).astype(np.float32)
+    table_np = O.f32_to_bf16_bits(t32) if dt == "bfloat16" else t32
+    table = _table_tensor(torch, table_np, dt, dev)
+    tdt = torch.bfloat16 if dt == "bfloat16" else torch.float32
+    gen = torch.Generator(device="cpu").manual_seed(9)
+    g = (1 + 0.1 * torch.randn(H, generator=gen)).to(tdt).to(dev)
+    b = (0.1 * torch.randn(H, generator=gen)).to(tdt).to(dev)
+    cfg = synth.WorkloadConfig("idx", (V - 1) // S, dt, 24, 1, 30, "1+poisson1", 1.1, num_slots=S)
+    batches = [synth.make_batch(cfg, seed=77)]
+    edge = {"user_offsets": np.array([0, 4])}
+    rng = np.random.default_rng(2)
+    for sl in range(1, S + 1):
+        ids = np.concatenate([np.array([0, -7, V + 5, 3], dtype=np.int64), rng.integers(0, V, 43)])
+        edge[sl] = (ids, np.array([0, 0, 4, 44, 47], dtype=np.int64))
+    batches.append(edge)
+    for batch in batches:
+        v64, o64 = _to_dev_batch(torch, batch, dev, slots=S)
+        v32, o32 = [v.to(torch.int32) for v in v64], [o.to(torch.int32) for o in o64]
+        r64 = _run_k1(torch, table, v64, o64, g, b, 1e-5)
+        r32 = _run_k1(torch, table, v32, o32, g, b, 1e-5)
+        for x, y in zip(r64, r32):
+            assert torch.equal(x, y)
+    with pytest.raises(ValueError):
+        device_ops.rep_gather_ln_quant(table, v32[:-1] + v64[-1:], o32, g, b, 1e-5)
+
+
 def test_dense_layernorm_quant_matches_fused(cuda_device):
     """rb_layernorm_quant on pooled rows == the fused kernel's LayerNorm/int8 stage."""
     import torch

@@ -2,6 +2,7 @@
 
 import numpy as np
 import pytest
+import torch
 
 from baidu_cti_grab_b200 import synth
 from baidu_cti_grab_b200.pipeline import pack_batch
@@ -68,3 +69,20 @@ def test_empty_batch_packs_as_one_empty_chunk():
     pb = pack_batch(b, pin=False, chunk_items=4)
     assert pb.num_items == 0 and pb.num_ids == 0 and len(pb.chunks) == 1
     assert pb.chunks[0].num_items == 0 and pb.host.numel() == 28  # 28 one-entry offset arrays
+
+
+def test_index_dtype_auto_int32_and_int64_fallback():
+    cfg = synth.WorkloadConfig("pack", 500, "bfloat16", 6, 1, 20, "1+poisson1", 1.1)
+    b = synth.make_batch(cfg, seed=8)
+    p32 = pack_batch(b, pin=False, chunk_items=5)
+    p64 = pack_batch(b, pin=False, chunk_items=5, index_dtype="int64")
+    assert p32.host.dtype == torch.int32 and p64.host.dtype == torch.int64
+    assert p32.nbytes * 2 == p64.nbytes
+    assert np.array_equal(p32.host.numpy().astype(np.int64), p64.host.numpy())
+    assert [c.lengths for c in p32.chunks] == [c.lengths for c in p64.chunks]
+    # an id beyond int32: auto keeps int64, an explicit int32 request is refused
+    v, o = b[7]
+    b[7] = (np.concatenate([v[:-1], np.array([1 << 33], dtype=np.int64)]), o)
+    assert pack_batch(b, pin=False, chunk_items=5).host.dtype == torch.int64
+    with pytest.raises(ValueError):
+        pack_batch(b, pin=False, index_dtype="int32")
