@@ -140,12 +140,16 @@ class HostPipeline:
     """Runs packed host batches through ``rep`` with H2D / compute / D2H overlapped.
 
     ``max_ids`` and ``max_items`` bound the batches (ids summed over slots,
-    items); ``max_chunks`` bounds the chunks per batch."""
+    items); ``max_chunks`` bounds the chunks per batch.  The last chunk of a
+    run is computed in ``tail_parts`` item ranges, each copied out as soon as
+    it is done, so that less of the final copy-out waits behind the kernels."""
 
     def __init__(self, rep: torch.nn.Module, max_ids: int, max_items: int, depth: int = 2,
-                 max_chunks: int = 16):
+                 max_chunks: int = 16, tail_parts: int = 4):
         dev = rep.emb.weight.device
         self.rep = rep
+        self.tail_parts = tail_parts
+        self._tail_events: List[torch.cuda.Event] = []
         self.device = dev
         self.depth = depth
         self.s_in = torch.cuda.Stream(dev)
@@ -172,6 +176,24 @@ class HostPipeline:
             self._chunk_events[(k, c)] = ev
         return ev
 
+    @staticmethod
+    def _tail_bounds(pb: PackedBatch, ch: PackedChunk, parts: int):
+        """Item ranges of the chunk and each slot's host offsets, or None when the
+        chunk cannot be split: too few items, or offsets that decrease or leave
+        their values (those are passed through whole, as given)."""
+        n = ch.num_items
+        parts = min(parts, n)
+        if parts <= 1:
+            return None
+        S = pb.num_slots
+        flat = pb.host[ch.start: ch.start + ch.size].numpy()
+        pos = np.cumsum([0] + ch.lengths)
+        offs = [flat[pos[S + s]: pos[S + s + 1]] for s in range(S)]
+        for s, o in enumerate(offs):
+            if len(o) != n + 1 or o[0] < 0 or o[-1] > ch.lengths[s] or np.any(np.diff(o) < 0):
+                return None
+        return [(j * n) // parts for j in range(parts + 1)], offs
+
     def run(self, batches: Sequence[PackedBatch], host_out: Sequence[torch.Tensor]) -> None:
         """Process ``batches``; result i goes to ``host_out[i]`` (pinned, [items_i, d_model]).
         Returns after the work is enqueued; synchronise the device (or ``self.s_out``) to wait."""
@@ -190,12 +212,35 @@ class HostPipeline:
                                                            non_blocking=True)
                     copied.record(self.s_in)
                 self.s_comp.wait_event(copied)
-                with torch.cuda.stream(self.s_comp):
-                    rep_encoder_forward(self.rep, unpack_device(inb, ch, pb.num_slots), out=outb[i0:i1])
-                    computed.record(self.s_comp)
-                self.s_out.wait_event(computed)
-                with torch.cuda.stream(self.s_out):
-                    host_out[i][i0:i1].copy_(outb[i0:i1], non_blocking=True)
+                views = unpack_device(inb, ch, pb.num_slots)
+                last = i == len(batches) - 1 and c == len(pb.chunks) - 1
+                tail = self._tail_bounds(pb, ch, self.tail_parts) if last else None
+                if tail is None:
+                    with torch.cuda.stream(self.s_comp):
+                        rep_encoder_forward(self.rep, views, out=outb[i0:i1])
+                        computed.record(self.s_comp)
+                    self.s_out.wait_event(computed)
+                    with torch.cuda.stream(self.s_out):
+                        host_out[i][i0:i1].copy_(outb[i0:i1], non_blocking=True)
+                    continue
+                # items [a, b) of the chunk: offsets stay absolute within the chunk's
+                # values; the values end where item b starts (or at the chunk's end)
+                bounds, offs = tail
+                while len(self._tail_events) < len(bounds) - 1:
+                    self._tail_events.append(torch.cuda.Event())
+                for j in range(len(bounds) - 1):
+                    a, b = bounds[j], bounds[j + 1]
+                    part = {}
+                    for s in range(1, pb.num_slots + 1):
+                        v, o = views[s]
+                        part[s] = (v if b == ch.num_items else v[: int(offs[s - 1][b])], o[a: b + 1])
+                    ev = self._tail_events[j]
+                    with torch.cuda.stream(self.s_comp):
+                        rep_encoder_forward(self.rep, part, out=outb[i0 + a: i0 + b])
+                        ev.record(self.s_comp)
+                    self.s_out.wait_event(ev)
+                    with torch.cuda.stream(self.s_out):
+                        host_out[i][i0 + a: i0 + b].copy_(outb[i0 + a: i0 + b], non_blocking=True)
             self.in_free[k].record(self.s_comp)
             self.out_free[k].record(self.s_out)
 

@@ -61,6 +61,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-chunk-items", type=int, default=None,
                     help="items per pipeline chunk on the e2e path (default: the pipeline's; 0: whole batches)")
+    ap.add_argument("--e2e-tail-parts", type=int, default=4,
+                    help="item ranges the last chunk of the e2e run is computed and copied out in (1: whole)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layout", choices=["users", "slot-sharded"], default="users",
                     help="users: each rank a batch of its own users with a full table (the default step); "
@@ -443,7 +445,7 @@ def b200_arm(args):
         chunk_items = DEFAULT_CHUNK_ITEMS if args.e2e_chunk_items is None else (args.e2e_chunk_items or None)
         packed = [pack_batch(b, chunk_items=chunk_items) for b in host_batches]
         max_ids = max(st[1] for st in stats)
-        pipe = HostPipeline(rep, max_ids=max_ids, max_items=n_items_max)
+        pipe = HostPipeline(rep, max_ids=max_ids, max_items=n_items_max, tail_parts=args.e2e_tail_parts)
         host_outs = [torch.empty((st[0], D_OUT), dtype=bf).pin_memory() for st in stats]
         seq = [packed[i % len(packed)] for i in range(K)]
         outs = [host_outs[i % len(host_outs)] for i in range(K)]
@@ -460,7 +462,7 @@ def b200_arm(args):
         e_ms = e0.elapsed_time(e1)
         e_items = sum(pb.num_items for pb in seq)
         e2e = [e_items, e_ms, sum(pb.nbytes for pb in seq) / K, sum(pb.num_items * D_OUT * 2 for pb in seq) / K,
-               chunk_items, str(seq[0].host.dtype).replace("torch.", "")]
+               chunk_items, str(seq[0].host.dtype).replace("torch.", ""), args.e2e_tail_parts]
 
     # ---- max over ranks
     vals = torch.tensor([ms, e2e[1] if e2e else 0.0, k1_ms, k2_ms], dtype=torch.float64, device=dev)
@@ -527,7 +529,7 @@ def b200_arm(args):
         if e2e is not None:
             line["e2e"] = {"value": round(e2e_items_all / (e2e_ms_max * 1e-3), 1), "unit": "items/s",
                            "h2d_bytes_per_step": int(e2e[2]), "d2h_bytes_per_step": int(e2e[3]),
-                           "chunk_items": e2e[4], "index_dtype": e2e[5],
+                           "chunk_items": e2e[4], "index_dtype": e2e[5], "tail_parts": e2e[6],
                            "api": "HostPipeline.run -> rep_encoder_forward (fuse_mode b200): per chunk of a batch's "
                                   "items one pinned H2D copy of its packed ids/offsets (int32 when they fit), "
                                   "K1 + K2, and one D2H copy of its bf16 output rows; copies of one chunk overlap "

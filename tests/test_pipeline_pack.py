@@ -86,3 +86,49 @@ def test_index_dtype_auto_int32_and_int64_fallback():
     assert pack_batch(b, pin=False, chunk_items=5).host.dtype == torch.int64
     with pytest.raises(ValueError):
         pack_batch(b, pin=False, index_dtype="int32")
+
+
+@pytest.mark.parametrize("chunk_items,parts", [(None, 4), (37, 4), (37, 3), (5, 8)])
+def test_tail_ranges_keep_every_bag(chunk_items, parts):
+    """The last chunk of a pipeline run is computed in item ranges: offsets
+    o[a:b+1] (absolute within the chunk) over values cut at o[b] give every
+    item the bag it has in the whole chunk."""
+    from baidu_cti_grab_b200.pipeline import HostPipeline
+
+    cfg = synth.WorkloadConfig("pack", 500, "bfloat16", 9, 1, 30, "1+poisson1", 1.1)
+    b = synth.make_batch(cfg, seed=12)
+    pb = pack_batch(b, pin=False, chunk_items=chunk_items)
+    ch = pb.chunks[-1]
+    tail = HostPipeline._tail_bounds(pb, ch, parts)
+    assert tail is not None
+    bounds, offs = tail
+    assert bounds[0] == 0 and bounds[-1] == ch.num_items and len(bounds) == min(parts, ch.num_items) + 1
+    flat = pb.host.numpy()[ch.start: ch.start + ch.size]
+    S = pb.num_slots
+    vals = np.split(flat, np.cumsum(ch.lengths)[:-1])[:S]
+    for s in range(S):
+        whole = _bags(vals[s], offs[s])
+        got = []
+        for a, bb in zip(bounds[:-1], bounds[1:]):
+            v = vals[s] if bb == ch.num_items else vals[s][: int(offs[s][bb])]
+            o = offs[s][a: bb + 1]
+            got.extend(v[int(o[i]): (int(o[i + 1]) if i + 1 < len(o) - 1 else len(v))] for i in range(len(o) - 1))
+        assert len(got) == len(whole)
+        for g, w in zip(got, whole):
+            assert np.array_equal(g, w)
+
+
+def test_tail_ranges_refuse_unsplittable_chunks():
+    from baidu_cti_grab_b200.pipeline import HostPipeline
+
+    cfg = synth.WorkloadConfig("pack", 500, "bfloat16", 3, 1, 3, "1+poisson1", 1.1)
+    b = synth.make_batch(cfg, seed=13)
+    pb = pack_batch(b, pin=False, chunk_items=None)
+    assert HostPipeline._tail_bounds(pb, pb.chunks[0], 1) is None  # one range: nothing to split
+    v, o = b[4]
+    o = o.copy()
+    if len(o) > 2:
+        o[1], o[2] = o[2] + 1, o[1]
+        b[4] = (v, o)
+        pb = pack_batch(b, pin=False, chunk_items=None)  # passed through as given
+        assert HostPipeline._tail_bounds(pb, pb.chunks[0], 2) is None
