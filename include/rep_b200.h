@@ -29,7 +29,7 @@ enum rb_act_mode { RB_ACT_DYNAMIC = 0, RB_ACT_STATIC = 1, RB_ACT_NONE = 2 };
 enum rb_status {
   RB_OK = 0,
   RB_ERR_VALUE = 1,       /* bad shape / argument  -> ValueError */
-  RB_ERR_UNSUPPORTED = 2, /* valid but not supported by this build -> ValueError */
+  RB_ERR_UNSUPPORTED = 2, /* valid but not supported by this library -> ValueError */
   RB_ERR_CUDA = 3,        /* CUDA runtime/driver error -> RuntimeError */
   RB_ERR_DEVICE = 4       /* not an sm_100 device, or a device-side timeout -> RuntimeError */
 };
