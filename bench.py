@@ -435,6 +435,12 @@ def b200_arm(args):
     n0 = stats[0][0]
     cublas_ms = time_cuda(lambda: torch._int_mm(q_buf[:n0], w_nk.t()), reps=5)
     cublas_tops = k2_ops(n0) / (cublas_ms * 1e-3) / 1e12
+    # and a square 8192^3 int8 GEMM: the library's int8 throughput on this GPU,
+    # a measured stand-in for the int8 peak that MEASURED_PEAKS.json lacks
+    sq = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device=dev)
+    sq_ms = time_cuda(lambda: torch._int_mm(sq, sq.t()), reps=5)
+    sq_tops = 2 * 8192 ** 3 / (sq_ms * 1e-3) / 1e12
+    del sq
 
     # ---- e2e through the public API from pinned host memory: packed host
     # batches, H2D / forward / D2H of successive batches overlapped on streams
@@ -497,6 +503,9 @@ def b200_arm(args):
                    "cublas_int8_same_shape": {"tops": round(cublas_tops, 1), "ms": round(cublas_ms, 4),
                                               "what": "torch._int_mm, int32 out without the epilogue, rank 0"},
                    "frac_vs_cublas_int8": round(k2_tops / cublas_tops, 4),
+                   "cublas_int8_square_8192": {"tops": round(sq_tops, 1), "ms": round(sq_ms, 4),
+                                               "what": "torch._int_mm 8192x8192x8192, int32 out, rank 0"},
+                   "frac_vs_cublas_int8_square": round(k2_tops / sq_tops, 4),
                    "traffic": None if k2_traffic is None else int(k2_traffic * n_mean),
                    "algorithmic_ops": int(k2_ops(int(n_mean))), "avg_ms": round(k2_ms_max, 4)}
         dominant = roof_k1 if k1_ms_max >= k2_ms_max else roof_k2
