@@ -713,12 +713,13 @@ __device__ __forceinline__ void epilogue_one(int32_t acc, int64_t m, int64_t n, 
 // (7.3 MB for the RepEncoder's linear), and a tensor-core tile would be 1/8
 // full.  One launch, no workspace.  A cluster of kGvSplit CTAs owns kGvCols
 // output columns; CTA r of the cluster covers the r-th 1/kGvSplit of K.  Warp w
-// owns columns 4w..4w+3 of the cluster and lane l the 16-byte K chunks l,
-// l+32, l+64, l+96 of each round of 128 chunks: a thread issues all sixteen of
-// its weight loads before the first product, so the whole weight is in flight
-// at once (the grid is resident in one wave), and the round's A slice
-// (M x 2 KB) comes into shared memory with cp.async.  Products are exact
-// dp4a; the warp's MT x 4 sums are reduce-scattered over its lanes, written
+// owns columns 4(w%4)..4(w%4)+3 of the cluster (for 9-16 rows, warps 4-7 take
+// rows 8-15 of the same columns) and lane l the 16-byte K chunks l, l+32,
+// l+64, l+96 of each round of 128 chunks: a thread issues all sixteen of its
+// weight loads before the first product, so the whole weight is in flight at
+// once (the grid is resident in one wave), and the round's A slice (M x 2 KB)
+// comes into shared memory with cp.async.  Products are exact dp4a; the warp's
+// rows x 4 sums are reduce-scattered over its lanes, written
 // into the leader CTA's shared memory through the cluster's distributed shared
 // memory, and summed there in CTA order before the usual epilogue.  int32
 // addition (modulo 2^32, like the tensor core's) is associative, so the result
@@ -726,7 +727,11 @@ __device__ __forceinline__ void epilogue_one(int32_t acc, int64_t m, int64_t n, 
 constexpr int kGemvMaxM = 16;
 constexpr int kGvSplit = 8;     // CTAs per cluster, along K
 constexpr int kGvCols = 16;     // output columns per cluster
-constexpr int kGvThreads = 128; // 4 warps x 4 columns
+constexpr int kGvThreads = 128; // 4 warps x 4 columns per group of rows
+// rows of A per group of 4 warps: 16 rows run as two groups of 8, so that a
+// thread carries 32 sums instead of 64 and twice the warps share an SM (the
+// M = 16 case is latency-bound on its dp4a chains at 167 registers per thread)
+__host__ __device__ constexpr int gv_groups(int mt) { return mt >= 16 ? 2 : 1; }
 constexpr int kGvIt = 4;        // chunks per lane per round
 constexpr int kGvRound = 32 * kGvIt;
 
@@ -736,17 +741,22 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 template <int MT>
-__global__ void __launch_bounds__(kGvThreads, 3)
+__global__ void __launch_bounds__(kGvThreads * gv_groups(MT), gv_groups(MT) > 1 ? 2 : 3)
     w8a8_gemv_kernel(const int8_t* __restrict__ A, int64_t lda, const int8_t* __restrict__ B, int64_t ldb,
                      const __grid_constant__ EpiParams ep) {
-  constexpr int V = MT * 4;  // sums per warp: rows x 4 columns
+  constexpr int kGroups = gv_groups(MT);
+  constexpr int RG = MT / kGroups;              // rows per group
+  constexpr int kThreads = kGvThreads * kGroups;
+  constexpr int V = RG * 4;                     // sums per warp: its group's rows x 4 columns
   __shared__ __align__(16) int4 sA[MT][kGvRound];
-  __shared__ __align__(16) uint32_t red[kGvSplit][4][V];
+  __shared__ __align__(16) uint32_t red[kGvSplit][4 * kGroups][V];
   // every CTA of the cluster has started before any writes into the leader's
   // shared memory (the matching wait comes after the products)
   asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   const uint32_t rank = pair::cluster_rank();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int cw = warp & 3;       // the warp's 4 columns: 4*cw .. 4*cw+3 of the cluster's 16
+  const int row0 = (warp >> 2) * RG;  // the warp's rows: row0 .. row0+RG-1
   const int64_t n0 = (int64_t)(blockIdx.x / kGvSplit) * kGvCols;
   const int M = (int)ep.M;
   const int64_t chunks = ep.K / 16;
@@ -755,12 +765,12 @@ __global__ void __launch_bounds__(kGvThreads, 3)
   const int64_t k_end = min(chunks, k0 + per_cta);
   // the leader's epilogue operands, requested now so that their latency
   // overlaps the loads and products instead of following the last barrier
-  constexpr int kPer = (MT * kGvCols + kGvThreads - 1) / kGvThreads;
+  constexpr int kPer = (MT * kGvCols + kThreads - 1) / kThreads;
   float e_sa[kPer], e_sb[kPer], e_bi[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     e_sa[j] = e_sb[j] = e_bi[j] = 0.0f;
-    const int o = threadIdx.x + j * kGvThreads;
+    const int o = threadIdx.x + j * kThreads;
     const int m = o / kGvCols;
     const int64_t n = n0 + o % kGvCols;
     if (rank == 0 && ep.out_dtype != RB_I32 && o < MT * kGvCols && m < M && n < ep.N) {
@@ -769,14 +779,14 @@ __global__ void __launch_bounds__(kGvThreads, 3)
       if (ep.bias != nullptr) e_bi[j] = load_as_f32(ep.bias, ep.bias_dtype, n);
     }
   }
-  int32_t acc[MT][4];
+  int32_t acc[RG][4];
 #pragma unroll
-  for (int m = 0; m < MT; ++m)
+  for (int m = 0; m < RG; ++m)
 #pragma unroll
     for (int c = 0; c < 4; ++c) acc[m][c] = 0;
   for (int64_t r0 = k0; r0 < k_end; r0 += kGvRound) {
     // A rows of this round into shared memory (zeros past M or the slice)
-    for (int i = threadIdx.x; i < MT * kGvRound; i += kGvThreads) {
+    for (int i = threadIdx.x; i < MT * kGvRound; i += kThreads) {
       const int m = i / kGvRound, q = i % kGvRound;
       const bool ok = m < M && r0 + q < k_end;
       cp_async16((uint32_t)__cvta_generic_to_shared(&sA[m][q]), ok ? A + m * lda + (r0 + q) * 16 : A, ok ? 16u : 0u);
@@ -788,7 +798,7 @@ __global__ void __launch_bounds__(kGvThreads, 3)
       const int64_t q = r0 + lane + 32 * it;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const int64_t n = n0 + 4 * warp + c;
+        const int64_t n = n0 + 4 * cw + c;
         b[it][c] = (q < k_end && n < ep.N) ? __ldg(reinterpret_cast<const int4*>(B + n * ldb) + q)
                                            : make_int4(0, 0, 0, 0);
       }
@@ -798,8 +808,8 @@ __global__ void __launch_bounds__(kGvThreads, 3)
 #pragma unroll
     for (int it = 0; it < kGvIt; ++it) {
 #pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        const int4 a = sA[m][lane + 32 * it];
+      for (int m = 0; m < RG; ++m) {
+        const int4 a = sA[row0 + m][lane + 32 * it];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           int v = acc[m][c];
@@ -819,7 +829,7 @@ __global__ void __launch_bounds__(kGvThreads, 3)
   // V <= 32, and on lane j / 2 for V = 64.
   uint32_t v[V];
 #pragma unroll
-  for (int m = 0; m < MT; ++m)
+  for (int m = 0; m < RG; ++m)
 #pragma unroll
     for (int c = 0; c < 4; ++c) v[4 * m + c] = (uint32_t)acc[m][c];
   int h = V;
@@ -858,13 +868,13 @@ __global__ void __launch_bounds__(kGvThreads, 3)
   if (rank != 0) return;
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
-    const int o = threadIdx.x + j * kGvThreads;
+    const int o = threadIdx.x + j * kThreads;
     const int m = o / kGvCols, col = o % kGvCols;
     const int64_t n = n0 + col;
     if (o < MT * kGvCols && m < M && n < ep.N) {
       uint32_t sum = 0;
 #pragma unroll
-      for (int r = 0; r < kGvSplit; ++r) sum += red[r][col >> 2][4 * m + (col & 3)];
+      for (int r = 0; r < kGvSplit; ++r) sum += red[r][(m / RG) * 4 + (col >> 2)][4 * (m % RG) + (col & 3)];
       if (ep.out_dtype == RB_I32) {
         reinterpret_cast<int32_t*>(ep.out)[m * ep.ldo + n] = (int32_t)sum;
         continue;
@@ -1018,7 +1028,7 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
   if (M <= kGemvMaxM) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(((N + kGvCols - 1) / kGvCols) * kGvSplit));
-    cfg.blockDim = dim3(kGvThreads);
+    cfg.blockDim = dim3(kGvThreads * (M > 8 ? gv_groups(16) : 1));
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
