@@ -107,6 +107,49 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_
       "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 
+// Operand kinds of the one-SM kernel.  Every kind consumes 32 bytes of K per
+// MMA (int8: 32 elements, bf16: 16, fp32 as tf32: 8) and a 128-byte swizzle row
+// per stage, so the shared-memory layout and descriptor steps are shared.
+enum GemmKind : int { kKindI8 = 0, kKindBF16 = 1, kKindTF32 = 2 };
+template <int KIND>
+struct KindTraits;
+template <>
+struct KindTraits<kKindI8> {
+  static constexpr int elt = 1;
+  static constexpr uint32_t idesc = IDESC;
+};
+template <>
+struct KindTraits<kKindBF16> {  // D = F32 (bits 4-5 = 1), A/B = BF16 (1), K-major
+  static constexpr int elt = 2;
+  static constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                    ((uint32_t)(BM >> 4) << 24);
+};
+template <>
+struct KindTraits<kKindTF32> {  // D = F32, A/B = TF32 (2), K-major
+  static constexpr int elt = 4;
+  static constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                    ((uint32_t)(BM >> 4) << 24);
+};
+
+template <int KIND>
+__device__ __forceinline__ void umma_kind(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+  if constexpr (KIND == kKindI8) {
+    umma_i8(d_tmem, adesc, bdesc, acc);
+  } else if constexpr (KIND == kKindBF16) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(KindTraits<KIND>::idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(KindTraits<KIND>::idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+  }
+}
+
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
@@ -164,6 +207,9 @@ __device__ __forceinline__ void ld_param8(const void* p, int dtype, int64_t i, F
 // Epilogue for 32 consecutive columns of one row: out = ((f32(acc) * sa) * sb) + bias,
 // one rounded fp32 operation at a time (pairs of columns per packed instruction).
 // Every array index is static, so the values stay in registers.
+// With kF32Acc (the floating-point kinds) the accumulator is fp32 and the
+// epilogue is out = acc + bias, without scales.
+template <bool kF32Acc = false>
 __device__ __forceinline__ void epilogue_32(const uint32_t* r, int64_t row, int64_t col0, float sa_v,
                                             const EpiParams& ep) {
   const int64_t N = ep.N;
@@ -181,20 +227,28 @@ __device__ __forceinline__ void epilogue_32(const uint32_t* r, int64_t row, int6
     }
     return;
   }
-  const F2 sa2 = f2(sa_v, sa_v);
   F2 v[16];
+  if constexpr (kF32Acc) {
 #pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = mul2(f2(__int2float_rn((int)r[2 * j]), __int2float_rn((int)r[2 * j + 1])), sa2);
+    for (int j = 0; j < 16; ++j) v[j] = f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+  } else {
+    const F2 sa2 = f2(sa_v, sa_v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      v[j] = mul2(f2(__int2float_rn((int)r[2 * j]), __int2float_rn((int)r[2 * j + 1])), sa2);
+  }
   const size_t osz = ep.out_dtype == RB_F32 ? 4 : 2;
-  const bool vec = ncol == 32 && aligned(ep.sb, 16) && (ep.bias == nullptr || aligned(ep.bias, 16)) &&
+  const bool vec = ncol == 32 && (kF32Acc || aligned(ep.sb, 16)) && (ep.bias == nullptr || aligned(ep.bias, 16)) &&
                    (col0 & 7) == 0 && ((uintptr_t)ep.out + (row * ep.ldo + col0) * osz) % 32 == 0;
   if (vec) {
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       F2 p[4];
-      ld_param8(ep.sb, ep.sb_dtype, col0 + 8 * g, p);
+      if constexpr (!kF32Acc) {
+        ld_param8(ep.sb, ep.sb_dtype, col0 + 8 * g, p);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) v[4 * g + k] = mul2(v[4 * g + k], p[k]);
+        for (int k = 0; k < 4; ++k) v[4 * g + k] = mul2(v[4 * g + k], p[k]);
+      }
       if (ep.bias != nullptr) {
         ld_param8(ep.bias, ep.bias_dtype, col0 + 8 * g, p);
 #pragma unroll
@@ -236,7 +290,7 @@ __device__ __forceinline__ void epilogue_32(const uint32_t* r, int64_t row, int6
     if (j >= ncol) break;
     const float2 x2 = un(v[j >> 1]);
     float x = (j & 1) ? x2.y : x2.x;
-    x = __fmul_rn(x, load_as_f32(ep.sb, ep.sb_dtype, col0 + j));
+    if constexpr (!kF32Acc) x = __fmul_rn(x, load_as_f32(ep.sb, ep.sb_dtype, col0 + j));
     if (ep.bias != nullptr) x = __fadd_rn(x, load_as_f32(ep.bias, ep.bias_dtype, col0 + j));
     const int64_t o = row * ep.ldo + col0 + j;
     if (ep.out_dtype == RB_F32) {
@@ -251,9 +305,10 @@ __device__ __forceinline__ void epilogue_32(const uint32_t* r, int64_t row, int6
   }
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
-    w8a8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ EpiParams ep) {
+template <int KIND>
+__device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmA, const CUtensorMap& tmB, const EpiParams& ep) {
+  constexpr int kElt = KindTraits<KIND>::elt;
+  constexpr bool kF32Acc = KIND != kKindI8;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
@@ -303,7 +358,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int64_t n_tiles = (ep.N + BN - 1) / BN;
   const int ksplits = ep.ksplits;
   const int64_t num_tiles = m_tiles * n_tiles * ksplits;
-  const int kblocks = (int)((ep.K + BK - 1) / BK);
+  const int kblocks = (int)((ep.K * kElt + BK - 1) / BK);
   // tile t -> split t % ksplits, n tile (t / ksplits) % n_tiles, m tile t / (ksplits * n_tiles);
   // split s covers k blocks [s*kblocks/ksplits, (s+1)*kblocks/ksplits)
   auto kb_begin = [&](int64_t t) { return (int)((t % ksplits) * kblocks / ksplits); };
@@ -328,8 +383,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           const uint32_t fb = smem_u32(&full[stage]);
           mbar_arrive_expect_tx(fb, STAGE_BYTES);
-          tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmA, kb * BK, m0, fb, pol_a);
-          tma_load_2d(smem_u32(sB + stage * B_BYTES), &tmB, kb * BK, n0, fb, pol_b);
+          tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmA, kb * (BK / kElt), m0, fb, pol_a);
+          tma_load_2d(smem_u32(sB + stage * B_BYTES), &tmB, kb * (BK / kElt), n0, fb, pol_b);
           issued |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -364,8 +419,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint64_t bdesc = sw128_desc(smem_u32(sB + stage * B_BYTES));
 #pragma unroll
           for (int k = 0; k < BK / MMA_K; ++k)
-            umma_i8(d_tmem, adesc + (uint64_t)(k * MMA_K / 16), bdesc + (uint64_t)(k * MMA_K / 16),
-                    (kb > kb0 || k > 0) ? 1u : 0u);
+            umma_kind<KIND>(d_tmem, adesc + (uint64_t)(k * MMA_K / 16), bdesc + (uint64_t)(k * MMA_K / 16),
+                            (kb > kb0 || k > 0) ? 1u : 0u);
           umma_commit(smem_u32(&empty[stage]));
           if (++stage == STAGES) {
             stage = 0;
@@ -397,7 +452,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int64_t row = m0 + quarter * 32 + lane;
       float sa_v = 0.0f;
-      if (row < ep.M && ep.out_dtype != RB_I32 && ksplits == 1)
+      if (!kF32Acc && row < ep.M && ep.out_dtype != RB_I32 && ksplits == 1)
         sa_v = load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? row : 0);
       if (ksplits > 1) pep.out = ep.partials + (tile % ksplits) * ep.M * ep.N;
 #pragma unroll 1
@@ -406,7 +461,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (col0 >= ep.N) break;  // warp-uniform
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-        if (row < ep.M) epilogue_32(r, row, col0, sa_v, ksplits > 1 ? pep : ep);
+        if (row < ep.M) epilogue_32<kF32Acc>(r, row, col0, sa_v, ksplits > 1 ? pep : ep);
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[acc]));
@@ -422,6 +477,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                  : "memory");
   }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    w8a8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ EpiParams ep) {
+  gemm_tc_body<kKindI8>(tmA, tmB, ep);
+}
+
+// bf16 x bf16 (kind::f16) or fp32 x fp32 (kind::tf32) with fp32 accumulators:
+// out = A B^T + bias, the unquantised Linear
+template <int KIND>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fp_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ EpiParams ep) {
+  gemm_tc_body<KIND>(tmA, tmB, ep);
 }
 
 // ----------------------------------------------------------------------------
@@ -921,6 +991,27 @@ __global__ void w8a8_gemm_simple_kernel(const int8_t* A, int64_t lda, const int8
   }
 }
 
+// CUDA-core fp GEMM for shapes the tensor-map path cannot take: fp32 sum of
+// products in K order, then + bias.  One thread per output element.
+template <typename T>
+__global__ void fp_gemm_simple_kernel(const T* A, int64_t lda, const T* B, int64_t ldb,
+                                      const __grid_constant__ EpiParams ep) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= ep.M * ep.N) return;
+  const int64_t m = idx / ep.N, n = idx % ep.N;
+  float acc = 0.0f;
+  for (int64_t k = 0; k < ep.K; ++k) acc = __fmaf_rn((float)A[m * lda + k], (float)B[n * ldb + k], acc);
+  if (ep.bias != nullptr) acc = __fadd_rn(acc, load_as_f32(ep.bias, ep.bias_dtype, n));
+  const int64_t o = m * ep.ldo + n;
+  if (ep.out_dtype == RB_F32) {
+    reinterpret_cast<float*>(ep.out)[o] = acc;
+  } else if (ep.out_dtype == RB_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(ep.out)[o] = __float2bfloat16_rn(acc);
+  } else {
+    reinterpret_cast<__half*>(ep.out)[o] = __float2half_rn(acc);
+  }
+}
+
 // --------------------------------------------------------------------- host
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
@@ -936,15 +1027,17 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return g_encode;
 }
 
-static int make_tmap(CUtensorMap* tm, const int8_t* base, int64_t inner, int64_t outer, int64_t ld_bytes,
-                     uint32_t box_inner, uint32_t box_outer) {
+// 2-D tensor map of a row-major [outer, inner] matrix (inner and box_inner in
+// elements of `dt`, ld_bytes the row pitch in bytes), 128-byte swizzle
+static int make_tmap(CUtensorMap* tm, const void* base, int64_t inner, int64_t outer, int64_t ld_bytes,
+                     uint32_t box_inner, uint32_t box_outer, CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8) {
   auto enc = encode_fn();
   if (enc == nullptr) return fail(RB_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)ld_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides, box, estr,
+  CUresult r = enc(tm, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(RB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -953,6 +1046,7 @@ static int make_tmap(CUtensorMap* tm, const int8_t* base, int64_t inner, int64_t
 
 static std::once_flag g_attr_once[64];
 static std::once_flag g_pair_attr_once[64];
+static std::once_flag g_fp_attr_once[64];
 
 }  // namespace tc
 }  // namespace rb
@@ -1120,21 +1214,94 @@ extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64
 }
 
 // ----------------------------------------------------------------------------
+// Unquantised Linear on the tensor cores: out = A B^T + bias with A [M, K] and
+// B [N, K] both bf16 (tcgen05 kind::f16) or both fp32 (kind::tf32: operands
+// rounded to tf32 by the tensor core, products accumulated in fp32), fp32
+// accumulators in TMEM, bias added in fp32, out in bf16 / fp16 / fp32.
+extern "C" int rb_fp_gemm(const void* A, int ab_dtype, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N,
+                          int64_t K, const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
+                          void* stream) {
+  using namespace rb::tc;
+  if (M < 0 || N < 0 || K < 0) return fail(RB_ERR_VALUE, "negative GEMM shape");
+  if (M == 0 || N == 0) return RB_OK;
+  if (ab_dtype != RB_BF16 && ab_dtype != RB_F32) return fail(RB_ERR_VALUE, "rb_fp_gemm operands must be bf16 or f32");
+  if (A == nullptr || B == nullptr || out == nullptr) return fail(RB_ERR_VALUE, "null operand");
+  if (lda < K || ldb < K || ldo < N) return fail(RB_ERR_VALUE, "leading dimension smaller than the row");
+  if (out_dtype != RB_BF16 && out_dtype != RB_F16 && out_dtype != RB_F32)
+    return fail(RB_ERR_VALUE, "out dtype must be bf16/f16/f32");
+  if (bias != nullptr && bias_dtype != RB_F32 && bias_dtype != RB_BF16 && bias_dtype != RB_F16)
+    return fail(RB_ERR_VALUE, "bias dtype must be f32/bf16/f16");
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL) return fail(RB_ERR_UNSUPPORTED, "dimension above 2^31-1");
+  if (!device_is_sm100()) return fail(RB_ERR_DEVICE, "rb_fp_gemm needs an sm_100 (B200) device");
+  EpiParams ep{};
+  ep.bias = bias;
+  ep.out = out;
+  ep.ldo = ldo;
+  ep.M = M;
+  ep.N = N;
+  ep.K = K;
+  ep.bias_dtype = bias_dtype;
+  ep.out_dtype = out_dtype;
+  ep.ksplits = 1;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int elt = ab_dtype == RB_BF16 ? 2 : 4;
+  // TMA needs 16-byte aligned bases and row pitches; K > 0
+  const bool tma_ok = K > 0 && (K * elt) % 16 == 0 && (lda * elt) % 16 == 0 && (ldb * elt) % 16 == 0 &&
+                      aligned(A, 16) && aligned(B, 16);
+  if (!tma_ok) {
+    const int64_t total = M * N;
+    const unsigned blocks = (unsigned)((total + 255) / 256);
+    if (ab_dtype == RB_BF16)
+      fp_gemm_simple_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(A), lda, static_cast<const __nv_bfloat16*>(B), ldb, ep);
+    else
+      fp_gemm_simple_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(A), lda,
+                                                           static_cast<const float*>(B), ldb, ep);
+    return check_cuda(cudaGetLastError(), "fp_gemm_simple_kernel launch");
+  }
+  const CUtensorMapDataType dt = ab_dtype == RB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUtensorMap tmA, tmB;
+  int rc = make_tmap(&tmA, A, K, M, lda * elt, BK / elt, BM, dt);
+  if (rc) return rc;
+  rc = make_tmap(&tmB, B, K, N, ldb * elt, BK / elt, BN, dt);
+  if (rc) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(g_fp_attr_once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(fp_gemm_tc_kernel<kKindBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    SMEM_BYTES);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(fp_gemm_tc_kernel<kKindTF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return check_cuda(attr_err, "cudaFuncSetAttribute(fp_gemm_tc_kernel)");
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = (int)std::min<int64_t>(tiles, sm_count());
+  if (ab_dtype == RB_BF16)
+    fp_gemm_tc_kernel<kKindBF16><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tmA, tmB, ep);
+  else
+    fp_gemm_tc_kernel<kKindTF32><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tmA, tmB, ep);
+  return check_cuda(cudaGetLastError(), "fp_gemm_tc_kernel launch");
+}
+
+// ----------------------------------------------------------------------------
 // Allocation-free entry point.  Some callers cannot allocate device memory on
-// their own: code that runs inside a CUDA-graph capture they do not control,
-// embedders whose memory is owned by another allocator (a framework pool, a
-// pre-sized arena in a latency-critical server), or plug-in hosts that forbid
-// cudaMalloc after start-up.  rb_w8a8_gemm_noalloc runs the same GEMM as
-// rb_w8a8_gemm_ws, taking its split-K workspace from the fixed device array
-// below instead of from the caller.
+// their own: embedders whose device memory belongs to another allocator (a
+// framework's caching pool, a pre-sized arena in a latency-critical server),
+// and plug-in hosts that forbid cudaMalloc once they have started.
+// rb_w8a8_gemm_noalloc runs the same GEMM as rb_w8a8_gemm_ws, taking its
+// split-K workspace from the fixed device array below instead of from the
+// caller.
 //
 // * The array lives for the life of the process on every GPU that loads this
 //   library: kNoAllocScratchElems int32 = 20 MiB.  Any shape on a 148-SM B200
 //   fits (the split heuristic never asks for more than 148 * 128 * 256 int32);
 //   a shape that would need more is rejected with RB_ERR_VALUE.
 // * The first call on a device looks up the array's device address with
-//   cudaGetSymbolAddress (with that device current) and caches it; make that
-//   first call before any stream capture that includes this entry point.
+//   cudaGetSymbolAddress (with that device current) and keeps it once the
+//   lookup has succeeded (a failed lookup is retried by the next call); make
+//   that first call before any stream capture that includes this entry point.
 // * All calls share the one array.  Every partial a call reads was written
 //   earlier in the same call, so nothing needs clearing between calls, but
 //   two calls that run at the same time on the GPU (other streams, other host
@@ -1142,9 +1309,8 @@ extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64
 // * It calls no cudaMalloc, cudaFree or allocating library routine.
 static constexpr int64_t kNoAllocScratchElems = 5 * 1024 * 1024;
 static __device__ __align__(256) int32_t g_gemm_noalloc_scratch[kNoAllocScratchElems];
-static int32_t* g_noalloc_scratch_ptr[64];
-static cudaError_t g_noalloc_scratch_err[64];
-static std::once_flag g_noalloc_scratch_once[64];
+static int32_t* g_noalloc_scratch_ptr[64];  // the array's device address, once looked up
+static std::mutex g_noalloc_scratch_mu;
 
 extern "C" int rb_w8a8_gemm_noalloc(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M,
                                     int64_t N, int64_t K, const void* sa, int sa_dtype, int sa_per_row,
@@ -1160,12 +1326,17 @@ extern "C" int rb_w8a8_gemm_noalloc(const int8_t* A, int64_t lda, const int8_t* 
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return check_cuda(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(RB_ERR_UNSUPPORTED, "device index %d out of range", dev);
-  std::call_once(g_noalloc_scratch_once[dev], [&] {
-    g_noalloc_scratch_err[dev] =
-        cudaGetSymbolAddress(reinterpret_cast<void**>(&g_noalloc_scratch_ptr[dev]), g_gemm_noalloc_scratch);
-  });
-  if (g_noalloc_scratch_err[dev] != cudaSuccess)
-    return check_cuda(g_noalloc_scratch_err[dev], "cudaGetSymbolAddress(g_gemm_noalloc_scratch)");
+  int32_t* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_scratch_mu);
+    if (g_noalloc_scratch_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_gemm_noalloc_scratch);
+      if (e != cudaSuccess) return check_cuda(e, "cudaGetSymbolAddress(g_gemm_noalloc_scratch)");
+      g_noalloc_scratch_ptr[dev] = static_cast<int32_t*>(p);
+    }
+    scratch = g_noalloc_scratch_ptr[dev];
+  }
   return rb_w8a8_gemm_ws(A, lda, B, ldb, M, N, K, sa, sa_dtype, sa_per_row, sb, sb_dtype, bias, bias_dtype, out,
-                         ldo, out_dtype, g_noalloc_scratch_ptr[dev], kNoAllocScratchElems, stream);
+                         ldo, out_dtype, scratch, kNoAllocScratchElems, stream);
 }

@@ -9,11 +9,15 @@
 // warp w owns slots 4w..4w+3, and lane l of a warp owns columns 8l..8l+7 and
 // 256+8l..256+8l+7 of each of its slots (two 16-byte vectors of a bf16 row).
 // The pooled row sits in shared memory in the row dtype (28 KB for bf16)
-// between the statistics, the normalisation and the quantiser.  Statistics use
-// the fixed ("canonical") reduction order stated in the oracle: lane partials
-// in column order, xor-butterfly 16..1 across the warp per slot, then an
-// xor-butterfly over the slots.  Every floating-point step is an explicit
-// round-to-nearest operation so the result is reproducible bit for bit.
+// between the statistics, the normalisation and the quantiser.  The LayerNorm
+// statistics follow ATen's CUDA LayerNorm (the kernel the reference's
+// nn.LayerNorm runs on the GPU): 128 Welford chains, chain c walking columns
+// 4c..4c+3 of every slot in order, a shuffle-down tree per 32 chains and a
+// fixed merge of the four groups, var = m2/H and rstd = rsqrtf(var + eps).
+// Two warps run the 128 chains, two per lane in packed fp32 pairs.  Every
+// floating-point step is an explicit round-to-nearest operation in the same
+// order as ATen's, so mean, rstd, the LayerNorm row and the int8 row equal
+// the reference's bit for bit.
 //
 // HBM traffic per item (bf16 table, k ids per slot): 28*k*1 KB of table rows
 // + 28*k*8 B ids + 28*2*8 B offsets (4 B each with int32 indices) + 14336 B
@@ -23,6 +27,7 @@
 namespace rb {
 
 constexpr int kSlotsPerWarp = 4;
+constexpr int kMaxWarps = (RB_MAX_SLOTS + kSlotsPerWarp - 1) / kSlotsPerWarp;
 #ifndef RB_K1_BF16_ROWS
 #define RB_K1_BF16_ROWS 2
 #endif
@@ -89,26 +94,6 @@ __device__ __forceinline__ uint32_t pack_i8x4_prmt(int a, int b, int c, int d) {
   const uint32_t ab = __byte_perm((uint32_t)a, (uint32_t)b, 0x0040);
   const uint32_t cd = __byte_perm((uint32_t)c, (uint32_t)d, 0x0040);
   return __byte_perm(ab, cd, 0x5410);
-}
-
-// Canonical butterfly of four slots' lane partials at once.  Each step adds
-// the same pairs as a per-slot xor-butterfly (16, 8, 4, 2, 1), but after the
-// first two steps a lane only carries the slot it will finish: lanes 0-7 end
-// with slot 0's total, 8-15 slot 1, 16-23 slot 2, 24-31 slot 3.
-__device__ __forceinline__ float warp_sum4_butterfly(float v0, float v1, float v2, float v3, int lane) {
-  const bool lo16 = lane < 16;
-  float k0 = lo16 ? v0 : v2, k1 = lo16 ? v1 : v3;
-  const float o0 = lo16 ? v2 : v0, o1 = lo16 ? v3 : v1;
-  k0 = __fadd_rn(k0, __shfl_xor_sync(0xffffffffu, o0, 16));
-  k1 = __fadd_rn(k1, __shfl_xor_sync(0xffffffffu, o1, 16));
-  const bool lo8 = (lane & 8) == 0;
-  float k = lo8 ? k0 : k1;
-  const float o = lo8 ? k1 : k0;
-  k = __fadd_rn(k, __shfl_xor_sync(0xffffffffu, o, 8));
-  k = __fadd_rn(k, __shfl_xor_sync(0xffffffffu, k, 4));
-  k = __fadd_rn(k, __shfl_xor_sync(0xffffffffu, k, 2));
-  k = __fadd_rn(k, __shfl_xor_sync(0xffffffffu, k, 1));
-  return k;
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -270,42 +255,88 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) 
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ int64_t shfl_i64(int64_t v, int src) {
+__device__ __forceinline__ int32_t shfl_idx(int32_t v, int src) { return __shfl_sync(0xffffffffu, v, src); }
+__device__ __forceinline__ int64_t shfl_idx(int64_t v, int src) {
   int lo = __shfl_sync(0xffffffffu, (int)(v & 0xffffffff), src);
   int hi = __shfl_sync(0xffffffffu, (int)(v >> 32), src);
   return ((int64_t)hi << 32) | (uint32_t)lo;
 }
 
-// a[j] for a runtime j in [0, 4) without dynamic register indexing
-template <typename V>
-__device__ __forceinline__ V sel4(const V* a, int j) {
-  return j == 0 ? a[0] : (j == 1 ? a[1] : (j == 2 ? a[2] : a[3]));
+// a[j] for a runtime j in [0, N) without dynamic register indexing
+template <int N, typename V>
+__device__ __forceinline__ V sel(const V* a, int j) {
+  V r = a[0];
+#pragma unroll
+  for (int i = 1; i < N; ++i)
+    if (j == i) r = a[i];
+  return r;
+}
+
+// ------------------------------------- LayerNorm statistics in ATen's order
+// ATen's CUDA LayerNorm forward (PyTorch aten/src/ATen/native/cuda/
+// layer_norm_kernel.cu: vectorized_layer_norm_kernel -> compute_stats,
+// cuWelfordOnlineSum, cuWelfordCombine; 128 threads per row) keeps one
+// Welford state per thread.  Thread c walks columns 4c..4c+3 of slot 0, then
+// of slot 1, ... (groups of 4 elements strided by 128 groups); each warp's 32
+// states are merged by shuffle-down (distances 16..1), then warps 0,1 merge
+// warps 2,3 and warp 0 merges warp 1.  Here a lane of warps 0-1 carries
+// chains c and c + 64 in the two halves of packed fp32 pairs.
+struct Welford2 {
+  F2 mean, m2;
+};
+
+// cuWelfordOnlineSum on both chains: r = 1/(count + 1), rounded once
+__device__ __forceinline__ void welford_push2(Welford2& s, F2 x, float r) {
+  const F2 delta = sub2(x, s.mean);
+  s.mean = fma2(delta, f2(r, r), s.mean);
+  s.m2 = fma2(delta, sub2(x, s.mean), s.m2);
+}
+
+// cuWelfordCombine(dataB = b, dataA = a) when both sides hold `cnt` elements:
+// delta = b.mean - a.mean, nA = nB = cnt * (1 / (2 cnt)),
+// mean = fma(nA, a.mean, nB * b.mean), m2 = fma(delta * delta * cnt, nB, a.m2 + b.m2)
+__device__ __forceinline__ Welford2 welford_merge2(const Welford2& b, const Welford2& a, float cnt) {
+  const float n = __fmul_rn(cnt, __fdiv_rn(1.0f, __fadd_rn(cnt, cnt)));
+  const F2 n2 = f2(n, n);
+  const F2 delta = sub2(b.mean, a.mean);
+  Welford2 o;
+  o.mean = fma2(n2, a.mean, mul2(n2, b.mean));
+  o.m2 = fma2(mul2(mul2(delta, delta), f2(cnt, cnt)), n2, add2(a.m2, b.m2));
+  return o;
+}
+
+__device__ __forceinline__ float2 welford_merge1(float b_mean, float b_m2, float a_mean, float a_m2, float cnt) {
+  const float n = __fmul_rn(cnt, __fdiv_rn(1.0f, __fadd_rn(cnt, cnt)));
+  const float delta = __fsub_rn(b_mean, a_mean);
+  const float mean = __fmaf_rn(n, a_mean, __fmul_rn(n, b_mean));
+  const float m2 = __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), cnt), n, __fadd_rn(a_m2, b_m2));
+  return make_float2(mean, m2);
 }
 
 // One CTA per item.  Warp w owns slots 4w..4w+3 and lane l owns 16 columns
 // of each (file header).  Per slot the warp sums the bag's table rows in bag
 // order (kRows rows in flight; the rows of the warp's id window were already
-// requested into L2 by bulk prefetches), rounds the sums to the row dtype into
-// the item's shared-memory row and, from the rounded values still in
-// registers, takes the slot sum T_s (lane partials, xor butterfly) and the
-// lane partials of Q_s = sum (x - T_s/512)^2.  After one barrier every warp
-// combines the slot statistics into mean and rstd itself, normalises its
-// slots in place (y rounded to the row dtype) with the absmax, and after a
-// second barrier quantises them to int8.  bf16 rows stay packed in shared
-// memory (28 KB per item) and enter fp32 arithmetic through the
-// mixed-precision add/sub.  TA is the storage type of gamma/beta (uint16_t
-// for bf16/fp16, float).  With bf16 rows the register budget (48 per
-// thread) keeps five 7-warp CTAs resident per SM: the gather's latency needs
-// that occupancy more than the code needs registers.  An fp32 row takes 56 KB
-// of shared memory, so at most three CTAs fit and the budget is larger.
+// requested into L2 by bulk prefetches) and rounds the sums to the row dtype
+// into the item's shared-memory row.  After a barrier warps 0-1 run the 128
+// LayerNorm chains of ATen's order over the row (lane l: chains l and l + 64 of
+// its warp's half, as a packed fp32 pair) and leave two merged states in shared
+// memory; after a second barrier every warp finishes the merge (mean, rstd)
+// itself, normalises its slots in place (y rounded to the row dtype) with the
+// absmax, and after a third barrier quantises them to int8.  bf16 rows stay
+// packed in shared memory (28 KB per item) and enter fp32 arithmetic through
+// the mixed-precision add/sub.  TA is the storage type of gamma/beta (uint16_t
+// for bf16/fp16, float).  With bf16 rows the register budget (48 per thread)
+// keeps five 7-warp CTAs resident per SM: the gather's latency, and the
+// chains' serial tail (112 dependent Welford steps), need that occupancy more
+// than the code needs registers.  An fp32 row takes 56 KB of shared memory, so
+// at most three CTAs fit and the budget is larger.
 template <typename T, int MODE, int kS, typename TA, typename IdxT>
 __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(const __grid_constant__ RepParams p) {
   constexpr bool kBf16 = sizeof(T) == 2;
   constexpr int kRows = kBf16 ? RB_K1_BF16_ROWS : 2;  // table rows a warp holds in registers
   extern __shared__ __align__(16) uint8_t s_raw[];
-  __shared__ float s_tot[RB_MAX_SLOTS];  // per-slot sums T_s
-  __shared__ float s_q[RB_MAX_SLOTS];    // per-slot centred square sums Q_s
-  __shared__ float s_wmax[8];
+  __shared__ float s_stat[4];  // Welford (mean, m2) of chain groups {0,2} and {1,3}
+  __shared__ float s_wmax[kMaxWarps];
   uint32_t* s_words = reinterpret_cast<uint32_t*>(s_raw);  // bf16 row: 256 words per slot
   float* s_f32 = reinterpret_cast<float*>(s_raw);          // fp32 row: 512 floats per slot
 
@@ -331,23 +362,12 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     }
   }
 
-  // lane partials of Q_s of the warp's slots (0 for slots past S)
-  float part[kSlotsPerWarp] = {0.0f, 0.0f, 0.0f, 0.0f};
-  auto put_part = [&](int j, float v) {
-#pragma unroll
-    for (int jj = 0; jj < kSlotsPerWarp; ++jj)
-      if (jj == j) part[jj] = v;
-  };
-
   // the warp's j-th slot is pooled in `acc` (fp32, not yet rounded): round it
-  // to T into shared memory (and the optional pooled output), then take the
-  // slot statistics from the rounded values
+  // to T into shared memory (and the optional pooled output)
   auto finish_slot = [&](int j, const float* acc) {
     const int s = slot_of(j);
-    float a0 = 0.0f, a1 = 0.0f;
-    uint32_t w[8];
-    F2 x[8];
     if constexpr (kBf16) {
+      uint32_t w[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
       st_words(s_words + s * 256, lane, w);
@@ -356,14 +376,8 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       } else if (p.pooled != nullptr) {
         st_words(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, w);
       }
-      if constexpr (MODE != kGatherPool) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          a0 = add_lo(a0, w[i]);
-          a1 = add_hi(a1, w[i]);
-        }
-      }
     } else {
+      F2 x[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) x[i] = f2(acc[2 * i], acc[2 * i + 1]);
       sts_pairs(s_f32, s, lane, x);
@@ -372,37 +386,6 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       } else if (p.pooled != nullptr) {
         stg_pairs(reinterpret_cast<float*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, x);
       }
-      if constexpr (MODE != kGatherPool) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          a0 = __fadd_rn(a0, acc[2 * i]);
-          a1 = __fadd_rn(a1, acc[2 * i + 1]);
-        }
-      }
-    }
-    if constexpr (MODE != kGatherPool) {
-      float tot = __fadd_rn(a0, a1);
-#pragma unroll
-      for (int d = 16; d >= 1; d >>= 1) tot = __fadd_rn(tot, __shfl_xor_sync(0xffffffffu, tot, d));
-      const float m = __fmul_rn(tot, 0.001953125f);  // T_s / 512, exact
-      F2 q = f2(0.0f, 0.0f);
-      if constexpr (kBf16) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const F2 d = f2(sub_lo(w[i], m), sub_hi(w[i], m));
-          q = fma2(d, d, q);
-        }
-      } else {
-        const F2 m2 = f2(m, m);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const F2 d = sub2(x[i], m2);
-          q = fma2(d, d, q);
-        }
-      }
-      const float2 qv = un(q);
-      put_part(j, __fadd_rn(qv.x, qv.y));
-      if (lane == 0) s_tot[s] = tot;
     }
   };
 
@@ -433,25 +416,27 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       finish_slot(j, acc);
     }
   } else {
-    // ---- bag bounds of this warp's slots: lanes 0-3 starts, lanes 4-7 ends
-    int64_t bound = 0;
+    // ---- bag bounds of this warp's slots: lanes 0..3 starts, lanes 4..7 ends
+    // bag positions fit the index type (int32 offsets address at most 2^31 ids)
+    IdxT bound = 0;
     {
-      const int j = lane & 3;
-      if (lane < 8 && j < nsl) {
+      const bool is_start = lane < kSlotsPerWarp;
+      const int j = is_start ? lane : lane - kSlotsPerWarp;
+      if (lane < 2 * kSlotsPerWarp && j < nsl) {
         const int s = slot_of(j);
         const int64_t nz = p.slots.nnz[s];
         const IdxT* off = static_cast<const IdxT*>(p.slots.offsets[s]);
-        const int64_t b = (lane < 4) ? (int64_t)off[item] : ((item + 1 < p.num_items) ? (int64_t)off[item + 1] : nz);
-        bound = b < 0 ? 0 : (b > nz ? nz : b);
+        const int64_t b = is_start ? (int64_t)off[item] : ((item + 1 < p.num_items) ? (int64_t)off[item + 1] : nz);
+        bound = (IdxT)(b < 0 ? 0 : (b > nz ? nz : b));
       }
     }
-    int64_t start[kSlotsPerWarp];
+    IdxT start[kSlotsPerWarp];
     int pre[kSlotsPerWarp + 1];
     int total = 0;
 #pragma unroll
     for (int j = 0; j < kSlotsPerWarp; ++j) {
-      start[j] = shfl_i64(bound, j);
-      const int64_t e = shfl_i64(bound, 4 + j);
+      start[j] = shfl_idx(bound, j);
+      const IdxT e = shfl_idx(bound, kSlotsPerWarp + j);
       pre[j] = total;
       total += (j < nsl && e > start[j]) ? (int)(e - start[j]) : 0;
     }
@@ -465,8 +450,12 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       const int t = w0 + lane;
       int id = 0;
       if (t < total) {
-        const int j = (t >= pre[1]) + (t >= pre[2]) + (t >= pre[3]);
-        const int64_t v = static_cast<const IdxT*>(p.slots.values[slot_of(j)])[sel4(start, j) + (t - sel4(pre, j))];
+        int j = 0;
+#pragma unroll
+        for (int i = 1; i < kSlotsPerWarp; ++i) j += t >= pre[i];
+        const int64_t v =
+            static_cast<const IdxT*>(p.slots.values[slot_of(j)])[(int64_t)sel<kSlotsPerWarp>(start, j) +
+                                                                 (t - sel<kSlotsPerWarp>(pre, j))];
         id = (int)(v < 0 ? 0 : (v > vmax ? vmax : v));
         if (id != 0) prefetch_l2_bulk(table + (int64_t)id * kDim, kDim * (int)sizeof(T));
       }
@@ -552,32 +541,59 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
   if constexpr (MODE != kGatherPool) {
     const float H = (float)(S * kDim);
     const bool bf_affine = p.ln_dtype == RB_BF16;
-    const float slot_q = warp_sum4_butterfly(part[0], part[1], part[2], part[3], lane);  // lanes 8j..: slot j
-    {
-      const int j = lane >> 3;
-      if ((lane & 7) == 0 && j < nsl) s_q[slot_of(j)] = slot_q;
-    }
-    // the first slot's gamma/beta are requested before the barrier
+    // the first slot's gamma/beta are requested before the barriers
     Affine<TA> aff;
     if (nsl > 0) aff.load(p, slot_of(0), lane);
+    __syncthreads();  // the item's pooled row is complete in shared memory
+    if (warp < 2) {
+      // chains u and u + 64 of the 128 (u = threadIdx.x), as the halves of one pair
+      const int u = threadIdx.x;
+      Welford2 st{f2(0.0f, 0.0f), f2(0.0f, 0.0f)};
+#pragma unroll
+      for (int k = 0; k < RB_MAX_SLOTS; ++k) {
+        if (k >= S) break;
+        float lo[4], hi[4];
+        if constexpr (kBf16) {
+          const uint2 a = *reinterpret_cast<const uint2*>(s_words + k * 256 + 2 * u);
+          const uint2 b = *reinterpret_cast<const uint2*>(s_words + k * 256 + 128 + 2 * u);
+          lo[0] = bf16_lo(a.x); lo[1] = bf16_hi(a.x); lo[2] = bf16_lo(a.y); lo[3] = bf16_hi(a.y);
+          hi[0] = bf16_lo(b.x); hi[1] = bf16_hi(b.x); hi[2] = bf16_lo(b.y); hi[3] = bf16_hi(b.y);
+        } else {
+          // fp32 rows are lane-major per slot (sts_pairs): columns 4u..4u+3 sit
+          // at chunk u & 1 of lane u >> 1, columns 256 + 4u.. two chunks later
+          const float* base = s_f32 + k * kDim + (u & 1) * 128 + 4 * (u >> 1);
+          const float4 a = *reinterpret_cast<const float4*>(base);
+          const float4 b = *reinterpret_cast<const float4*>(base + 256);
+          lo[0] = a.x; lo[1] = a.y; lo[2] = a.z; lo[3] = a.w;
+          hi[0] = b.x; hi[1] = b.y; hi[2] = b.z; hi[3] = b.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) welford_push2(st, f2(lo[e], hi[e]), 1.0f / (float)(4 * k + e + 1));
+      }
+      float cnt = (float)(4 * S);
+#pragma unroll
+      for (int d = 16; d >= 1; d >>= 1) {
+        Welford2 o;
+        o.mean.r = __shfl_down_sync(0xffffffffu, st.mean.r, d);
+        o.m2.r = __shfl_down_sync(0xffffffffu, st.m2.r, d);
+        st = welford_merge2(st, o, cnt);
+        cnt = __fadd_rn(cnt, cnt);
+      }
+      if (lane == 0) {  // lo: chains of ATen warp `warp`, hi: of ATen warp `warp + 2`
+        const float2 m = un(st.mean), q = un(st.m2);
+        const float2 r = welford_merge1(m.x, q.x, m.y, q.y, cnt);
+        s_stat[2 * warp] = r.x;
+        s_stat[2 * warp + 1] = r.y;
+      }
+    }
     __syncthreads();
-    // every warp combines the slots itself (lane s holds slot s; lanes past S
-    // contribute zero): xor-butterfly of the slot sums -> mean, then of
-    // Q_s + 512 (m_s - mean)^2 (Chan's parallel update) -> M2
     float mean, rstd;
     {
-      const float t_l = lane < S ? s_tot[lane] : 0.0f;
-      const float q_l = lane < S ? s_q[lane] : 0.0f;
-      float t = t_l;
-#pragma unroll
-      for (int d = 16; d >= 1; d >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, d));
-      mean = __fdiv_rn(t, H);
-      const float dm = __fsub_rn(__fmul_rn(t_l, 0.001953125f), mean);
-      float c = lane < S ? __fadd_rn(q_l, __fmul_rn(512.0f, __fmul_rn(dm, dm))) : 0.0f;
-#pragma unroll
-      for (int d = 16; d >= 1; d >>= 1) c = __fadd_rn(c, __shfl_xor_sync(0xffffffffu, c, d));
-      const float var = __fdiv_rn(c, H);
-      rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
+      // ATen warp 0 (+2) merges warp 1 (+3); each side holds H / 2 elements
+      const float2 r = welford_merge1(s_stat[0], s_stat[1], s_stat[2], s_stat[3], 0.5f * H);
+      mean = r.x;
+      const float var = __fdiv_rn(r.y, H);
+      rstd = rsqrtf(__fadd_rn(var, p.eps));  // the CUDA function ATen's LayerNorm calls
     }
     const F2 mean2 = f2(mean, mean);
     const F2 rstd2 = f2(rstd, rstd);
@@ -699,7 +715,8 @@ static int fill_slots(SlotArgs& sa, const void* const* values, const void* const
 template <int MODE, typename IdxT = int64_t>
 static int launch_rep(const RepParams& p, int row_dtype, cudaStream_t stream) {
   if (p.num_items == 0) return RB_OK;
-  const int warps = (p.num_slots + kSlotsPerWarp - 1) / kSlotsPerWarp;
+  // a warp per 4 slots, and at least the 2 warps that run the LayerNorm chains
+  const int warps = max(2, (p.num_slots + kSlotsPerWarp - 1) / kSlotsPerWarp);
   dim3 grid((unsigned)p.num_items), block(32 * warps);
   // the item's pooled row: packed bf16, or fp32 for fp32 tables
   const size_t smem = (size_t)p.num_slots * kDim * dtype_size(row_dtype);
@@ -769,7 +786,9 @@ static int gather_ln_quant(const void* table, int table_dtype, int64_t num_rows,
   if (table_dtype != RB_BF16 && table_dtype != RB_F32)
     return fail(RB_ERR_VALUE, "table dtype must be RB_BF16 or RB_F32");
   if (table == nullptr || !aligned(table, 16)) return fail(RB_ERR_VALUE, "table must be 16-byte aligned");
-  if (num_rows < 1) return fail(RB_ERR_VALUE, "num_rows must be >= 1");
+  if (num_rows < 1 || num_rows > 0x7fffffffLL)
+    return fail(RB_ERR_VALUE, "num_rows must be in [1, 2^31-1] (ids are clamped in 32 bits), got %lld",
+                (long long)num_rows);
   if (slot_nnz == nullptr) return fail(RB_ERR_VALUE, "slot_nnz must be given");
   if (num_items == 0) return RB_OK;  // empty batch: nothing to read or write
   rc = check_ln_args(ln_gamma, ln_beta, ln_dtype, act_mode, static_scale, static_scale_dtype, q_out, ldq,
@@ -839,7 +858,9 @@ extern "C" int rb_rep_gather_pool(const void* table, int table_dtype, int64_t nu
   if (table_dtype != RB_BF16 && table_dtype != RB_F32)
     return fail(RB_ERR_VALUE, "table dtype must be RB_BF16 or RB_F32");
   if (table == nullptr || !aligned(table, 16)) return fail(RB_ERR_VALUE, "table must be 16-byte aligned");
-  if (num_rows < 1) return fail(RB_ERR_VALUE, "num_rows must be >= 1");
+  if (num_rows < 1 || num_rows > 0x7fffffffLL)
+    return fail(RB_ERR_VALUE, "num_rows must be in [1, 2^31-1] (ids are clamped in 32 bits), got %lld",
+                (long long)num_rows);
   if (slot_nnz == nullptr || col_slot == nullptr) return fail(RB_ERR_VALUE, "slot_nnz/col_slot must be given");
   if (num_items == 0) return RB_OK;
   if (pooled_out == nullptr || !aligned(pooled_out, 16))
@@ -873,7 +894,9 @@ extern "C" int rb_rep_gather_pool_scatter(const void* table, int table_dtype, in
   if (table_dtype != RB_BF16 && table_dtype != RB_F32)
     return fail(RB_ERR_VALUE, "table dtype must be RB_BF16 or RB_F32");
   if (table == nullptr || !aligned(table, 16)) return fail(RB_ERR_VALUE, "table must be 16-byte aligned");
-  if (num_rows < 1) return fail(RB_ERR_VALUE, "num_rows must be >= 1");
+  if (num_rows < 1 || num_rows > 0x7fffffffLL)
+    return fail(RB_ERR_VALUE, "num_rows must be in [1, 2^31-1] (ids are clamped in 32 bits), got %lld",
+                (long long)num_rows);
   if (slot_nnz == nullptr || col_slot == nullptr) return fail(RB_ERR_VALUE, "slot_nnz/col_slot must be given");
   if (num_dest < 1 || num_dest > RB_MAX_DEST)
     return fail(RB_ERR_VALUE, "num_dest must be in [1, %d], got %d", RB_MAX_DEST, num_dest);

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import ctypes
 import weakref
-from typing import Optional, Sequence, Tuple
+from typing import Dict, Optional, Sequence, Tuple
 
 import torch
 
@@ -334,6 +334,29 @@ def as_nk(qweight_t: torch.Tensor) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------- GEMM
+_WS_SIZE: Dict[Tuple[int, int, int], int] = {}
+_WS: Dict[Tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace_elems(M: int, N: int, K: int) -> int:
+    key = (M, N, K)
+    n = _WS_SIZE.get(key)
+    if n is None:
+        n = _WS_SIZE[key] = int(L.load().rb_w8a8_gemm_workspace_size(M, N, K))
+    return n
+
+
+def _workspace(dev: torch.device, elems: int) -> torch.Tensor:
+    """The split-K workspace of the current stream on `dev`, grown on demand.
+    One buffer per (device, stream): launches on one stream run in order, so
+    consecutive GEMMs on a stream can share it."""
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < elems:
+        ws = _WS[key] = torch.empty((elems,), dtype=torch.int32, device=dev)
+    return ws
+
+
 def w8a8_gemm(a: torch.Tensor, b_nk: torch.Tensor, scale_a: Optional[torch.Tensor],
               scale_b: Optional[torch.Tensor], out: torch.Tensor, *, bias: Optional[torch.Tensor] = None,
               sa_per_row: bool = True) -> torch.Tensor:
@@ -353,14 +376,38 @@ def w8a8_gemm(a: torch.Tensor, b_nk: torch.Tensor, scale_a: Optional[torch.Tenso
         scale_b = scale_b.contiguous()
     if bias is not None:
         bias = bias.contiguous()
-    ws_elems = int(L.load().rb_w8a8_gemm_workspace_size(M, N, K))
-    ws = torch.empty((ws_elems,), dtype=torch.int32, device=dev) if ws_elems > 0 else None
+    ws_elems = _workspace_elems(M, N, K)
+    ws = _workspace(dev, ws_elems) if ws_elems > 0 else None
     with torch.cuda.device(dev):
         L.call("rb_w8a8_gemm_ws", a.data_ptr(), a.stride(0), b_nk.data_ptr(), b_nk.stride(0), M, N, K,
                _ptr(scale_a), rb_dtype(scale_a) if scale_a is not None else 0, 1 if sa_per_row else 0,
                _ptr(scale_b), rb_dtype(scale_b) if scale_b is not None else 0, _ptr(bias),
                rb_dtype(bias) if bias is not None else 0, out.data_ptr(), out.stride(0), rb_dtype(out),
                _ptr(ws), ws_elems, _stream(dev))
+    return out
+
+
+def fp_gemm(a: torch.Tensor, b_nk: torch.Tensor, out: torch.Tensor, *,
+            bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = A @ B^T + bias on the tensor cores: A [M, K], B [N, K] both bf16
+    (kind::f16) or both fp32 (kind::tf32), fp32 accumulation."""
+    dev = require_cuda("fp_gemm", a, b_nk, out, bias)
+    if a.dim() != 2 or b_nk.dim() != 2 or a.stride(1) != 1 or b_nk.stride(1) != 1 or out.stride(1) != 1:
+        raise ValueError("fp_gemm expects row-major 2-D operands")
+    if a.dtype != b_nk.dtype or a.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("fp_gemm operands must both be bf16 or both fp32")
+    M, K = a.shape
+    N = b_nk.shape[0]
+    if b_nk.shape[1] != K:
+        raise ValueError(f"shape mismatch: A K={K}, B K={b_nk.shape[1]}")
+    if tuple(out.shape) != (M, N):
+        raise ValueError(f"out must be [{M}, {N}]")
+    if bias is not None:
+        bias = bias.contiguous()
+    with torch.cuda.device(dev):
+        L.call("rb_fp_gemm", a.data_ptr(), rb_dtype(a), a.stride(0), b_nk.data_ptr(), b_nk.stride(0), M, N, K,
+               _ptr(bias), rb_dtype(bias) if bias is not None else 0, out.data_ptr(), out.stride(0), rb_dtype(out),
+               _stream(dev))
     return out
 
 

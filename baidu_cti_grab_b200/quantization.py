@@ -8,7 +8,7 @@ Replaced entry points (reference file:line):
   w8a8_linear_triton_dynamic_unfused   :281-348  (_w8a8_matmul_kernel :38-105)
   w8a8_linear_triton_dynamic_fused     :351-404  (_w8a8_dynamic_fused_kernel :108-188)
   w8a8_linear_dynamic                  :407-408
-  bf16_linear / max_abs_diff / mean_abs_diff  :411-424
+  bf16_linear / max_abs_diff / mean_abs_diff  :411-424  (bf16_linear on rb_fp_gemm)
 
 This version rounds with ``trunc(x/scale +- 0.5)`` into [-127, 127] and takes
 the weight as W[N, K] (already K-contiguous).  The reference's "fused" kernel
@@ -22,7 +22,6 @@ compatibility; tile shapes are chosen by the kernel.
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from . import device_ops
 
@@ -94,8 +93,15 @@ def w8a8_linear_dynamic(*args, **kwargs):
 
 
 def bf16_linear(x, weight, bias=None):
-    return F.linear(x.to(torch.bfloat16), weight.to(torch.bfloat16),
-                    None if bias is None else bias.to(torch.bfloat16))
+    """The bf16 Linear the W8A8 path is compared with: x [..., K] and W [N, K] in
+    bf16 on the tcgen05 kind::f16 GEMM (fp32 accumulation), output bf16."""
+    if not x.is_cuda:
+        raise RuntimeError("bf16_linear expects CUDA tensors")
+    x2 = x.to(torch.bfloat16).reshape(-1, x.shape[-1]).contiguous()
+    w = weight.to(torch.bfloat16).contiguous()
+    out = torch.empty((x2.shape[0], w.shape[0]), dtype=torch.bfloat16, device=x.device)
+    device_ops.fp_gemm(x2, w, out, bias=None if bias is None else bias.to(torch.bfloat16))
+    return out.view(*x.shape[:-1], w.shape[0])
 
 
 def max_abs_diff(a, b):

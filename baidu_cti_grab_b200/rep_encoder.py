@@ -34,24 +34,52 @@ from . import device_ops
 FUSE_MODE = "b200"
 
 
+# pinned staging buffer per (device, index dtype) for host-resident slot arrays,
+# with the event of the last copy out of it
+_STAGING: Dict[tuple, tuple] = {}
+
+
+def _stage_to_device(host: Sequence[torch.Tensor], dtype: torch.dtype, device: torch.device):
+    """Copy host tensors to `device` as one contiguous transfer through a reused
+    pinned buffer: one H2D copy instead of one synchronous pageable copy per
+    array.  Returns the device views, in order."""
+    sizes = [t.numel() for t in host]
+    total = sum(sizes)
+    key = (device.index, dtype)
+    buf, done = _STAGING.get(key, (None, None))
+    if done is not None:
+        done.synchronize()  # the previous copy out of the buffer has finished
+    if buf is None or buf.numel() < total:
+        buf = torch.empty((max(total, 1),), dtype=dtype, pin_memory=True)
+    pos = 0
+    for t, n in zip(host, sizes):
+        buf[pos:pos + n].copy_(t.reshape(-1))
+        pos += n
+    flat = torch.empty((total,), dtype=dtype, device=device)
+    flat.copy_(buf[:total], non_blocking=True)
+    done = torch.cuda.Event()
+    done.record(torch.cuda.current_stream(device))
+    _STAGING[key] = (buf, done)
+    return list(torch.split(flat, sizes))
+
+
 def _slot_tensors(batch, slot_num: int, device: torch.device):
     """Device values/offsets of every slot: int32 when the batch holds only int32
     arrays (the packed ingestion format, half the bytes), else int64 as in the
-    reference's collate."""
-    values, offsets = [], []
+    reference's collate.  Arrays still on the host (the reference moves a CPU
+    offsets tensor to the values' device, models.py:31) travel in one staged copy."""
+    arrays = []
     for i in range(slot_num):
         v, o = batch[i + 1]
-        if not torch.is_tensor(v):
-            v = torch.as_tensor(v)
-        if not torch.is_tensor(o):
-            o = torch.as_tensor(o)
-        if v.device != device:
-            v = v.to(device, non_blocking=True)
-        values.append(v)
-        offsets.append(o.to(v.device))  # models.py:31
-    all32 = all(t.dtype == torch.int32 for t in values + offsets)
-    idx = torch.int32 if all32 else torch.int64
-    return ([v.to(idx).contiguous() for v in values], [o.to(idx).contiguous() for o in offsets])
+        arrays.append(v if torch.is_tensor(v) else torch.as_tensor(v))
+        arrays.append(o if torch.is_tensor(o) else torch.as_tensor(o))
+    idx = torch.int32 if all(t.dtype == torch.int32 for t in arrays) else torch.int64
+    on_host = [k for k, t in enumerate(arrays) if t.device != device]
+    if on_host:
+        for k, t in zip(on_host, _stage_to_device([arrays[k] for k in on_host], idx, device)):
+            arrays[k] = t
+    arrays = [t if t.dtype == idx and t.is_contiguous() else t.to(idx).contiguous() for t in arrays]
+    return arrays[0::2], arrays[1::2]
 
 
 def _quantized_weight(rep: nn.Module):

@@ -25,8 +25,9 @@ import torch
 from . import _lib, device_ops
 from .w8a8_preprocess import QuantizedWeight
 
+
 def flatten_input(x: torch.Tensor):
-    """Flatten [..., K] -> [M, K] and keep the original leading shape."""
+    """(x as a contiguous 2-D [rows, K] view, the leading dimensions to restore afterwards)."""
     return x.contiguous().view(-1, x.shape[-1]), x.shape[:-1]
 
 
@@ -100,7 +101,7 @@ def w8a8_scaled_mm_out(xq_2d: torch.Tensor, qweight: QuantizedWeight, scale_a: t
 
 def w8a8_scaled_mm(xq_2d: torch.Tensor, qweight: QuantizedWeight, scale_a: torch.Tensor, *,
                    bias: torch.Tensor | None = None, out_dtype: torch.dtype, static_act: bool) -> torch.Tensor:
-    """Run only the quantized int8 GEMM + scale multiply stage."""
+    """int8 A x the quantised weight on the tcgen05 GEMM, with the fp32 scale / bias epilogue fused."""
     assert xq_2d.ndim == 2
     K = xq_2d.shape[1]
     assert K == qweight.qweight_t.shape[0]
@@ -128,7 +129,7 @@ def int8_mm_no_scale_out(xq_2d: torch.Tensor, qweight: QuantizedWeight, out_2d: 
 
 
 def int8_mm_no_scale(xq_2d: torch.Tensor, qweight: QuantizedWeight, *, out_dtype: torch.dtype) -> torch.Tensor:
-    """Run int8 GEMM without dequant scales, for timing the dot stage only."""
+    """Raw int32 accumulators of int8 A x the quantised weight (no scales, no bias)."""
     assert xq_2d.ndim == 2
     K = xq_2d.shape[1]
     assert K == qweight.qweight_t.shape[0]
@@ -140,7 +141,8 @@ def int8_mm_no_scale(xq_2d: torch.Tensor, qweight: QuantizedWeight, *, out_dtype
 
 def w8a8_linear(x: torch.Tensor, qweight: QuantizedWeight, *, bias: torch.Tensor | None = None, act_mode: str,
                 static_act_scale: torch.Tensor | None = None) -> torch.Tensor:
-    """Run W8A8 Linear on x with arbitrary leading batch dimensions."""
+    """y = W8A8 Linear(x) for x of shape [..., K]: quantise the activations (static
+    per-tensor or dynamic per-token), int8 GEMM, fp32 epilogue, y in x.dtype."""
     assert x.shape[-1] == qweight.qweight_t.shape[0]
     x_2d, original_batch_shape = flatten_input(x)
     xq, scale_a = quantize_activation(x_2d, act_mode=act_mode, static_act_scale=static_act_scale)

@@ -233,13 +233,31 @@ int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, 
                     int32_t* workspace, int64_t workspace_elems, void* stream);
 
 /*
+ * Unquantised Linear on the tensor cores: out[m,n] = sum_k A[m,k] * B[n,k] + bias[n].
+ * Replaces the GEMM of kernels/rep_encoder_fusion.py:33-112 (_layernorm_linear_kernel,
+ * a tl.dot of bf16 operands -- or fp32 operands, which Triton multiplies as tf32 --
+ * with fp32 accumulation, then + bias) behind layernorm_linear_triton (:169-243).
+ *   A   [M, lda], B [N, ldb]: both RB_BF16 (tcgen05 kind::f16) or both RB_F32
+ *       (kind::tf32); K contiguous.  16-byte aligned bases and row pitches take
+ *       the TMA / tensor-core path; other layouts a CUDA-core kernel.
+ *   accumulators fp32 (TMEM), bias [N] f32/bf16/f16 or NULL added in fp32,
+ *   out [M, ldo] RB_BF16 / RB_F16 / RB_F32.
+ * Floating-point sums: results agree with an fp32 matmul of the same operands
+ * to within fp32 accumulation error (tf32 rounding of the operands for f32).
+ */
+int rb_fp_gemm(const void* A, int ab_dtype, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N,
+               int64_t K, const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
+               void* stream);
+
+/*
  * rb_w8a8_gemm_ws for callers that cannot allocate device memory themselves
- * (inside a graph capture they do not own, under another allocator's pool, in
- * hosts that forbid cudaMalloc after start-up).  No counterpart in the
- * reference.  The split-K workspace comes from a fixed 20 MiB device array in
+ * (their device memory belongs to another allocator's pool or a pre-sized
+ * arena, or their host forbids cudaMalloc after start-up).  No counterpart in
+ * the reference.  The split-K workspace comes from a fixed 20 MiB device array in
  * the library (held on every GPU that loads it); shapes needing more are
  * rejected with RB_ERR_VALUE.  The first call on a device resolves the array's
- * address (make it before any stream capture).  Calls share the array, so
+ * address and keeps it once resolved (make that call before any stream
+ * capture).  Calls share the array, so
  * calls that overlap on the GPU race; no state carries from one call to the
  * next.  Same results as rb_w8a8_gemm, bit for bit; allocates nothing.
  */

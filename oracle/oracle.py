@@ -22,7 +22,7 @@ LIB_PATH = os.path.join(HERE, "librep_oracle.so")
 
 F32, BF16, F16, I32 = 0, 1, 2, 3
 _DT = {"float32": F32, "bfloat16": BF16, "float16": F16}
-MAX_SLOTS = 32  # the canonical LayerNorm combines the slots by a 32-wide butterfly
+MAX_SLOTS = 32  # the widest row the CUDA kernels take (32 slots x 512)
 
 _lib = None
 
@@ -42,19 +42,20 @@ def lib():
         L = ctypes.CDLL(LIB_PATH)
         vp, i64, i32, f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
         L.rbo_embedding_bag_sum.argtypes = [vp, i32, i64, i64, vp, i64, vp, i64, vp, i32]
-        L.rbo_layernorm_row.argtypes = [vp, i64, vp, vp, f32, i32, vp, vp, vp]
+        L.rbo_layernorm_stats_rows.argtypes = [vp, i64, i64, f32, vp, vp]
+        L.rbo_layernorm_apply_rows.argtypes = [vp, i64, i64, vp, vp, vp, vp, i32, vp]
         L.rbo_quant_dynamic_v2.argtypes = [vp, i64, i64, vp, vp]
         L.rbo_quant_static_v2.argtypes = [vp, i64, f32, vp]
         L.rbo_quant_rows_v1.argtypes = [vp, i64, i64, vp, vp]
         L.rbo_gemm_i8_i32.argtypes = [vp, vp, i64, i64, i64, vp]
         L.rbo_scaled_epilogue.argtypes = [vp, i64, i64, vp, i32, vp, vp, i32, vp]
-        L.rbo_rep_forward.argtypes = [vp, i32, i64, vp, vp, vp, i64, i64, vp, vp, f32, i32, f32, vp,
-                                      vp, vp, vp, i32]
+        L.rbo_rep_pool_stats.argtypes = [vp, i32, i64, vp, vp, vp, i64, i64, f32, vp, vp, vp, i32]
+        L.rbo_rep_finish.argtypes = [vp, i32, i64, i64, vp, vp, vp, vp, i32, f32, vp, vp, vp, i32]
         L.rbo_round_to_dtype.argtypes = [vp, i64, i32, vp]
         L.rbo_dtype_to_f32.argtypes = [vp, i64, i32, vp]
-        for fn in (L.rbo_embedding_bag_sum, L.rbo_layernorm_row, L.rbo_quant_dynamic_v2,
-                   L.rbo_quant_static_v2, L.rbo_quant_rows_v1, L.rbo_gemm_i8_i32,
-                   L.rbo_scaled_epilogue, L.rbo_rep_forward, L.rbo_round_to_dtype,
+        for fn in (L.rbo_embedding_bag_sum, L.rbo_layernorm_stats_rows, L.rbo_layernorm_apply_rows,
+                   L.rbo_quant_dynamic_v2, L.rbo_quant_static_v2, L.rbo_quant_rows_v1, L.rbo_gemm_i8_i32,
+                   L.rbo_scaled_epilogue, L.rbo_rep_pool_stats, L.rbo_rep_finish, L.rbo_round_to_dtype,
                    L.rbo_dtype_to_f32):
             fn.restype = None
         _lib = L
@@ -107,23 +108,43 @@ def embedding_bag_sum(table: np.ndarray, table_dtype: str, values: np.ndarray, o
 
 
 # -------------------------------------------------------------- LayerNorm
+def rsqrt_nearest(v: np.ndarray) -> np.ndarray:
+    """Correctly rounded fp32 1/sqrt(v): the CPU-only stand-in for CUDA's rsqrtf,
+    which ATen's LayerNorm calls and which differs from it by up to 2 ulp."""
+    return (1.0 / np.sqrt(np.asarray(v, dtype=np.float64))).astype(np.float32)
+
+
+def _rstd(var_eps: np.ndarray, rsqrt) -> np.ndarray:
+    r = rsqrt_nearest(var_eps) if rsqrt is None else np.asarray(rsqrt(var_eps), dtype=np.float32)
+    return np.ascontiguousarray(r.reshape(var_eps.shape), dtype=np.float32)
+
+
+def layernorm_stats(x: np.ndarray, eps: float) -> Tuple[np.ndarray, np.ndarray]:
+    """Per-row mean and fl(var + eps) of rows x[M, H] (H % 4 == 0) in ATen CUDA's order."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m, h = x.shape
+    if h % 4 != 0:
+        raise ValueError(f"row width {h} is not a multiple of 4")
+    mean = np.empty(m, dtype=np.float32)
+    var_eps = np.empty(m, dtype=np.float32)
+    lib().rbo_layernorm_stats_rows(_p(x), m, h, eps, _p(mean), _p(var_eps))
+    return mean, var_eps
+
+
 def layernorm_rows(x: np.ndarray, gamma: np.ndarray, beta: np.ndarray, eps: float,
-                   out_dtype: str) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
-    """Canonical-order LayerNorm of rows x[M, S*512] (fp32 values of the row dtype)."""
+                   out_dtype: str, rsqrt=None) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """nn.LayerNorm of rows x[M, H] (fp32 values of the row dtype) as ATen's CUDA
+    kernel computes it.  ``rsqrt`` maps fl(var + eps) to rstd: pass the GPU's
+    rsqrtf (e.g. torch.rsqrt on a CUDA tensor) for bit-exact parity; the default
+    is the correctly rounded value.  Returns (y, mean, rstd)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     gamma = np.ascontiguousarray(gamma, dtype=np.float32)
     beta = np.ascontiguousarray(beta, dtype=np.float32)
     m, h = x.shape
-    if h % 512 != 0 or not 1 <= h // 512 <= MAX_SLOTS:
-        raise ValueError(f"row width {h} is not 512 x [1, {MAX_SLOTS}] slots")
+    mean, var_eps = layernorm_stats(x, eps)
+    rstd = _rstd(var_eps, rsqrt)
     y = np.empty_like(x)
-    mean = np.empty(m, dtype=np.float32)
-    rstd = np.empty(m, dtype=np.float32)
-    L = lib()
-    for r in range(m):
-        L.rbo_layernorm_row(_p(x[r]), h // 512, _p(gamma), _p(beta), eps, _DT[out_dtype],
-                            _p(y[r]), mean[r:].ctypes.data_as(ctypes.c_void_p),
-                            rstd[r:].ctypes.data_as(ctypes.c_void_p))
+    lib().rbo_layernorm_apply_rows(_p(x), m, h, _p(mean), _p(rstd), _p(gamma), _p(beta), _DT[out_dtype], _p(y))
     return y, mean, rstd
 
 
@@ -197,9 +218,10 @@ def scaled_epilogue(acc: np.ndarray, sa: np.ndarray, sb: np.ndarray, bias: Optio
 def rep_forward(table: np.ndarray, table_dtype: str, batch: Dict[object, object], gamma: np.ndarray,
                 beta: np.ndarray, eps: float = 1e-5, act_mode: str = "dynamic",
                 static_scale: float = 1.0, num_slots: Optional[int] = None,
-                intermediates: bool = False, threads: int = 0):
+                intermediates: bool = False, threads: int = 0, rsqrt=None):
     """gather -> pool -> concat -> LayerNorm -> int8 quant for a batch dict of numpy arrays.
 
+    ``rsqrt`` maps each row's fl(var + eps) to rstd (see layernorm_rows).
     Returns (q int8[N,H], scale fp32[N]) and, with intermediates=True, also the
     pooled and LayerNorm rows (fp32 values of the row dtype)."""
     if num_slots is None:
@@ -218,15 +240,19 @@ def rep_forward(table: np.ndarray, table_dtype: str, batch: Dict[object, object]
     beta = np.ascontiguousarray(beta, dtype=np.float32)
     q = np.empty((n, h), dtype=np.int8)
     scale = np.zeros(n, dtype=np.float32)
-    pooled = np.empty((n, h), dtype=np.float32) if intermediates else None
+    pooled = np.empty((n, h), dtype=np.float32)
+    mean = np.empty(n, dtype=np.float32)
+    var_eps = np.empty(n, dtype=np.float32)
     ln = np.empty((n, h), dtype=np.float32) if intermediates else None
     if threads <= 0:
         threads = max(1, min(os.cpu_count() or 1, 64))
-    lib().rbo_rep_forward(_p(table), _DT[table_dtype], table.shape[0], vp, op, _p(nnz), num_slots, n,
-                          _p(gamma), _p(beta), eps, 0 if act_mode == "dynamic" else 1,
-                          float(np.float32(static_scale)), _p(q), _p(scale),
-                          _p(pooled) if intermediates else None,
-                          _p(ln) if intermediates else None, threads)
+    L = lib()
+    L.rbo_rep_pool_stats(_p(table), _DT[table_dtype], table.shape[0], vp, op, _p(nnz), num_slots, n, eps,
+                         _p(pooled), _p(mean), _p(var_eps), threads)
+    rstd = _rstd(var_eps, rsqrt)
+    L.rbo_rep_finish(_p(pooled), _DT[table_dtype], num_slots, n, _p(mean), _p(rstd), _p(gamma), _p(beta),
+                     0 if act_mode == "dynamic" else 1, float(np.float32(static_scale)), _p(q), _p(scale),
+                     _p(ln) if intermediates else None, threads)
     if intermediates:
         return q, scale, pooled, ln
     return q, scale

@@ -17,34 +17,45 @@
  *                           accumulation in bag order, one RNE round to the
  *                           table dtype.  The last bag runs to the end of
  *                           `values` (offsets[:-1] is what the reference passes).
- *   rbo_layernorm_row       models.py:21,45 nn.LayerNorm(S*D, eps) over the
- *                           concatenated row, restated as a two-pass fp32
- *                           LayerNorm whose reduction order is fixed (the
- *                           "canonical order" below) so it is reproducible.
+ *   rbo_layernorm_stats     models.py:21,45 nn.LayerNorm(S*D, eps) over the
+ *   rbo_layernorm_apply     concatenated row, as ATen's CUDA LayerNorm
+ *                           computes it (order below).
  *   rbo_quant_dynamic_v2    quantization/w8a8_triton_kernels.py:41-64
  *   rbo_quant_static_v2     quantization/w8a8_triton_kernels.py:23-38
  *   rbo_quant_rows_v1       kernels/quantization.py:6-35
  *   rbo_gemm_i8_i32         quantization/w8a8_triton_kernels.py:67-171 (int32 acc)
  *   rbo_scaled_epilogue     quantization/w8a8_triton_kernels.py:230-246
- *   rbo_rep_forward         models.py:24-48 + w8a8_linear's quantiser, i.e.
- *                           gather -> pool -> concat -> LN -> int8 quant.
+ *   rbo_rep_pool_stats      models.py:24-45 gather -> pool -> concat and the
+ *   rbo_rep_finish          LayerNorm statistics; then LayerNorm + w8a8_linear's
+ *                           int8 quantiser once rstd is known (see below).
  *
- * Canonical LayerNorm reduction order (shared with the CUDA kernel): a row of
- * S slots x 512 columns is reduced slot by slot.  Inside a slot, "lane" l
- * (0..31) owns 16 elements, columns 8l..8l+7 then 256+8l..256+8l+7; walking
- * them in that order, elements at even positions accumulate into a0 and odd
- * positions into a1 (both from 0.0f), and the lane partial is a0 + a1; the
- * 32 lane partials are combined by an xor-butterfly with distances 16, 8, 4,
- * 2, 1 (p[l] = p[l] + p[l^d]).  (The even/odd split is what a packed two-wide
- * fp32 add computes.)  Per slot s this order gives the sum T_s of x and, with
- * the slot mean m_s = T_s / 512, the centred square sum Q_s of (x - m_s)^2
- * (fmaf(d, d, acc) per element).  The slots are then combined by the same
- * 32-wide xor-butterfly, slot s in position s and 0.0f in positions S..31:
- *   mean = butterfly_s(T_s) / H
- *   M2   = butterfly_s(Q_s + 512 * (m_s - mean)^2)   (Chan's parallel update)
- *   var  = M2 / H;  rstd = 1.0f / sqrtf(var + eps)
- *   y    = fmaf(rstd * (x - mean), gamma, beta)   (then RNE to the row dtype)
- * Division and square root are IEEE correctly rounded here and in the kernel.
+ * LayerNorm order.  The reference's nn.LayerNorm runs ATen's CUDA kernel on
+ * the GPU (PyTorch, not vendored by the reference: it pins torch 2.6.0 and
+ * this build runs 2.11.0; aten/src/ATen/native/cuda/layer_norm_kernel.cu,
+ * vectorized_layer_norm_kernel -> compute_stats, taken for rows whose length
+ * is a multiple of 4 with aligned buffers, which every RepEncoder row is).
+ * Its published algorithm, restated:
+ *   * 128 threads per row (4 warps of 32).  Thread t walks the 4-element
+ *     groups g = t, t+128, t+256, ... (elements 4g..4g+3 in order) with
+ *     Welford's online update, state (mean, m2, count) from zeros:
+ *       delta = x - mean; count = count + 1; r = 1/count (IEEE);
+ *       mean = fma(delta, r, mean); m2 = fma(delta, x - mean_new, m2)
+ *   * each warp combines its 32 states by shuffle-down with distances
+ *     16, 8, 4, 2, 1 (lane l takes lane l+d), combine(B = own, A = other):
+ *       delta = B.mean - A.mean; n = A.count + B.count; c = 1/n (IEEE);
+ *       nA = A.count*c; nB = B.count*c; mean = fma(nA, A.mean, nB*B.mean);
+ *       m2 = fma(delta*delta*A.count, nB, A.m2 + B.m2)
+ *   * warps 0,1 take warps 2,3, then warp 0 takes warp 1 (same combine);
+ *   * var = m2 / H (IEEE); rstd = rsqrtf(var + eps);
+ *   * y = fma(gamma, rstd * (x - mean), beta), rounded to the row dtype.
+ * rsqrtf is CUDA's hardware reciprocal square root (within 2 ulp, and not
+ * correctly rounded on about a quarter of inputs), so this file does not
+ * compute it: rbo_rep_pool_stats returns fl(var + eps) per row and the caller
+ * supplies rstd (evaluated on the GPU by the GPU tests; the CPU-only default
+ * in oracle.py is the correctly rounded value, which matches the GPU's to
+ * within 2 ulp).  With that one value supplied, mean, rstd and every output
+ * element equal ATen CUDA's bit for bit (pinned by tests/golden/ln_aten_cuda.npz,
+ * recorded from ATen on a B200 by tests/golden/gen_golden_aten_cuda.py).
  */
 #include <stdint.h>
 #include <string.h>
@@ -176,72 +187,81 @@ void rbo_embedding_bag_sum(const void* table, int table_dtype, int64_t num_rows,
     free(acc);
 }
 
-/* --------------------------------------------------- canonical LayerNorm */
-/* p[0] after the xor-butterfly p[l] = p[l] + p[l^d], d = 16, 8, 4, 2, 1 */
-static float butterfly32(float* p) {
-    for (int dist = 16; dist >= 1; dist >>= 1) {
-        float q[32];
-        for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ dist];
-        memcpy(p, q, 32 * sizeof(float));
-    }
-    return p[0];
+/* --------------------------------------------- LayerNorm (ATen CUDA order) */
+typedef struct { float mean, m2, count; } welford;
+
+/* layer_norm_kernel.cu cuWelfordOnlineSum */
+static inline welford welford_push(welford s, float x) {
+    welford o;
+    const float delta = x - s.mean;
+    o.count = s.count + 1.0f;
+    o.mean = fmaf(delta, 1.0f / o.count, s.mean);
+    o.m2 = fmaf(delta, x - o.mean, s.m2);
+    return o;
 }
 
-static float canonical_slot_sum(const float* seg, float mean, int centred) {
-    float p[32];
-    for (int l = 0; l < 32; ++l) {
-        /* lane l's 16 columns in order; even positions feed a0, odd positions a1 */
-        float a[2] = {0.0f, 0.0f};
-        for (int e = 0; e < 16; ++e) {
-            const int col = (e < 8) ? 8 * l + e : 256 + 8 * l + (e - 8);
-            float v = seg[col];
-            if (centred) {
-                float d = v - mean;
-                a[e & 1] = fmaf(d, d, a[e & 1]);
-            } else {
-                a[e & 1] = a[e & 1] + v;
-            }
-        }
-        p[l] = a[0] + a[1];
+/* layer_norm_kernel.cu cuWelfordCombine(dataB = b, dataA = a) */
+static inline welford welford_merge(welford b, welford a) {
+    welford o;
+    o.count = a.count + b.count;
+    if (o.count > 0.0f) {
+        const float delta = b.mean - a.mean;
+        const float c = 1.0f / o.count;
+        const float na = a.count * c, nb = b.count * c;
+        o.mean = fmaf(na, a.mean, nb * b.mean);
+        o.m2 = fmaf(delta * delta * a.count, nb, a.m2 + b.m2);
+    } else {
+        o.mean = 0.0f;
+        o.m2 = 0.0f;
     }
-    return butterfly32(p);
+    return o;
 }
 
 /*
- * LayerNorm of one row x[S*512] (values already in the row dtype, widened to
- * fp32).  gamma/beta widened to fp32.  y receives fp32 values rounded to
- * out_dtype (so y[] holds exactly what the kernel stores).  mean/rstd out.
- * 1 <= n_slots <= 32 (the slots are combined by a 32-wide butterfly).
+ * Mean and fl(var + eps) of one row x[H] (H % 4 == 0) in ATen CUDA's order
+ * (file header).  var_eps is the argument of the rsqrtf that gives rstd.
  */
-void rbo_layernorm_row(const float* x, int64_t n_slots, const float* gamma, const float* beta,
-                       float eps, int out_dtype, float* y, float* mean_out, float* rstd_out) {
-    const int64_t H = n_slots * 512;
-    float slot_sum[32], slot_q[32], p[32];
-    for (int64_t s = 0; s < 32; ++s) {
-        slot_sum[s] = 0.0f;
-        slot_q[s] = 0.0f;
+void rbo_layernorm_stats(const float* x, int64_t H, float eps, float* mean_out, float* var_eps_out) {
+    welford th[128], warp_state[4];
+    const int64_t groups = H / 4;
+    for (int t = 0; t < 128; ++t) {
+        welford s = {0.0f, 0.0f, 0.0f};
+        for (int64_t g = t; g < groups; g += 128)
+            for (int e = 0; e < 4; ++e) s = welford_push(s, x[4 * g + e]);
+        th[t] = s;
     }
-    for (int64_t s = 0; s < n_slots; ++s) {
-        slot_sum[s] = canonical_slot_sum(x + s * 512, 0.0f, 0);
-        const float m_s = slot_sum[s] / 512.0f;
-        slot_q[s] = canonical_slot_sum(x + s * 512, m_s, 1);
+    for (int w = 0; w < 4; ++w) {
+        welford l[32], n[32];
+        memcpy(l, th + 32 * w, sizeof(l));
+        for (int d = 16; d >= 1; d >>= 1) {
+            /* a lane past the warp reads its own state (shuffle-down semantics) */
+            for (int i = 0; i < 32; ++i) n[i] = welford_merge(l[i], i + d < 32 ? l[i + d] : l[i]);
+            memcpy(l, n, sizeof(l));
+        }
+        warp_state[w] = l[0];
     }
-    memcpy(p, slot_sum, sizeof(p));
-    const float mean = butterfly32(p) / (float)H;
-    /* Chan's combination of the per-slot centred sums, butterfly over slots */
-    for (int64_t s = 0; s < 32; ++s) {
-        const float d = slot_sum[s] / 512.0f - mean;
-        p[s] = s < n_slots ? slot_q[s] + 512.0f * (d * d) : 0.0f;
-    }
-    const float var = butterfly32(p) / (float)H;
-    const float rstd = 1.0f / sqrtf(var + eps);
-    for (int64_t k = 0; k < H; ++k) {
-        float d = x[k] - mean;
-        float t = rstd * d;
-        y[k] = round_to(out_dtype, fmaf(t, gamma[k], beta[k]));
-    }
-    if (mean_out) *mean_out = mean;
-    if (rstd_out) *rstd_out = rstd;
+    warp_state[0] = welford_merge(warp_state[0], warp_state[2]);
+    warp_state[1] = welford_merge(warp_state[1], warp_state[3]);
+    warp_state[0] = welford_merge(warp_state[0], warp_state[1]);
+    *mean_out = warp_state[0].mean;
+    *var_eps_out = warp_state[0].m2 / (float)H + eps;
+}
+
+/* y[k] = round_to(out_dtype, fma(gamma[k], rstd * (x[k] - mean), beta[k])) */
+void rbo_layernorm_apply(const float* x, int64_t H, float mean, float rstd, const float* gamma,
+                         const float* beta, int out_dtype, float* y) {
+    for (int64_t k = 0; k < H; ++k) y[k] = round_to(out_dtype, fmaf(gamma[k], rstd * (x[k] - mean), beta[k]));
+}
+
+/* Statistics of rows x[M, H]: mean[M] and fl(var + eps)[M]. */
+void rbo_layernorm_stats_rows(const float* x, int64_t M, int64_t H, float eps, float* mean, float* var_eps) {
+    for (int64_t r = 0; r < M; ++r) rbo_layernorm_stats(x + r * H, H, eps, mean + r, var_eps + r);
+}
+
+/* LayerNorm of rows x[M, H] given per-row mean and rstd. */
+void rbo_layernorm_apply_rows(const float* x, int64_t M, int64_t H, const float* mean, const float* rstd,
+                              const float* gamma, const float* beta, int out_dtype, float* y) {
+    for (int64_t r = 0; r < M; ++r) rbo_layernorm_apply(x + r * H, H, mean[r], rstd[r], gamma, beta, out_dtype, y + r * H);
 }
 
 /* ------------------------------------------------------------ quantisers */
@@ -324,21 +344,23 @@ void rbo_scaled_epilogue(const int32_t* acc, int64_t M, int64_t N, const float* 
 }
 
 /* -------------------------------------------------- whole RepEncoder row */
+/* Items [begin, end) of a batch are split over POSIX threads; results do not
+ * depend on the thread count. */
 typedef struct {
     const void* table; int table_dtype; int64_t num_rows;
     const int64_t* const* values; const int64_t* const* offsets; const int64_t* nnz;
     int64_t n_slots, n_items, begin, end;
-    const float* gamma; const float* beta; float eps; int act_mode; float static_scale;
-    int8_t* q; float* scale; float* pooled_out; float* ln_out;
+    float eps; float* pooled; float* mean; float* var_eps;
+    const float* rstd; const float* gamma; const float* beta; int act_mode; float static_scale;
+    int8_t* q; float* scale; float* ln_out;
 } rep_job;
 
-static void* rep_worker(void* arg) {
+static void* pool_stats_worker(void* arg) {
     const rep_job* jb = (const rep_job*)arg;
     const int64_t D = 512, H = jb->n_slots * D;
-    float* row = (float*)malloc(sizeof(float) * (size_t)H);
-    float* y = (float*)malloc(sizeof(float) * (size_t)H);
     float* acc = (float*)malloc(sizeof(float) * (size_t)D);
     for (int64_t i = jb->begin; i < jb->end; ++i) {
+        float* row = jb->pooled + i * H;
         for (int64_t s = 0; s < jb->n_slots; ++s) {
             const int64_t* off = jb->offsets[s];
             const int64_t nz = jb->nnz[s];
@@ -358,56 +380,83 @@ static void* rep_worker(void* arg) {
             }
             for (int64_t d = 0; d < D; ++d) row[s * D + d] = round_to(jb->table_dtype, acc[d]);
         }
-        rbo_layernorm_row(row, jb->n_slots, jb->gamma, jb->beta, jb->eps, jb->table_dtype, y, NULL, NULL);
+        rbo_layernorm_stats(row, H, jb->eps, jb->mean + i, jb->var_eps + i);
+    }
+    free(acc);
+    return NULL;
+}
+
+static void* finish_worker(void* arg) {
+    const rep_job* jb = (const rep_job*)arg;
+    const int64_t H = jb->n_slots * 512;
+    float* y = (float*)malloc(sizeof(float) * (size_t)H);
+    for (int64_t i = jb->begin; i < jb->end; ++i) {
+        rbo_layernorm_apply(jb->pooled + i * H, H, jb->mean[i], jb->rstd[i], jb->gamma, jb->beta,
+                            jb->table_dtype, y);
         if (jb->act_mode == 0) {
             rbo_quant_dynamic_v2(y, 1, H, jb->q + i * H, jb->scale + i);
         } else {
             rbo_quant_static_v2(y, H, jb->static_scale, jb->q + i * H);
         }
-        if (jb->pooled_out) memcpy(jb->pooled_out + i * H, row, sizeof(float) * (size_t)H);
         if (jb->ln_out) memcpy(jb->ln_out + i * H, y, sizeof(float) * (size_t)H);
     }
-    free(row);
     free(y);
-    free(acc);
     return NULL;
 }
 
-/*
- * gather -> pool (table dtype) -> concat -> LayerNorm (row dtype = table
- * dtype) -> dynamic (act_mode 0) or static (act_mode 1) int8 quantisation.
- * values/offsets/nnz are per-slot arrays.  Optional outputs pooled/ln
- * receive fp32 copies of the row-dtype intermediates [N, S*512].  Items are
- * split over n_threads POSIX threads; results do not depend on n_threads.
- */
-void rbo_rep_forward(const void* table, int table_dtype, int64_t num_rows,
-                     const int64_t* const* values, const int64_t* const* offsets, const int64_t* nnz,
-                     int64_t n_slots, int64_t n_items, const float* gamma, const float* beta, float eps,
-                     int act_mode, float static_scale, int8_t* q, float* scale,
-                     float* pooled_out, float* ln_out, int n_threads) {
+static void run_jobs(rep_job proto, int n_threads, void* (*fn)(void*)) {
     if (n_threads < 1) n_threads = 1;
     if (n_threads > 256) n_threads = 256;
     pthread_t th[256];
     rep_job jobs[256];
-    int64_t chunk = (n_items + n_threads - 1) / n_threads;
-    int started = 0;
+    int ok[256];
+    const int64_t chunk = (proto.n_items + n_threads - 1) / n_threads;
     for (int t = 0; t < n_threads; ++t) {
-        rep_job jb = {table, table_dtype, num_rows, values, offsets, nnz, n_slots, n_items,
-                      t * chunk, (t + 1) * chunk, gamma, beta, eps, act_mode, static_scale,
-                      q, scale, pooled_out, ln_out};
-        if (jb.begin > n_items) jb.begin = n_items;
-        if (jb.end > n_items) jb.end = n_items;
-        jobs[t] = jb;
+        jobs[t] = proto;
+        jobs[t].begin = t * chunk < proto.n_items ? t * chunk : proto.n_items;
+        jobs[t].end = (t + 1) * chunk < proto.n_items ? (t + 1) * chunk : proto.n_items;
     }
     for (int t = 1; t < n_threads; ++t) {
-        if (pthread_create(&th[t], NULL, rep_worker, &jobs[t]) == 0) {
-            started = t;
-        } else {
-            rep_worker(&jobs[t]);
-            th[t] = 0;
-        }
+        ok[t] = pthread_create(&th[t], NULL, fn, &jobs[t]) == 0;
+        if (!ok[t]) fn(&jobs[t]);
     }
-    rep_worker(&jobs[0]);
-    for (int t = 1; t <= started; ++t)
-        if (th[t]) pthread_join(th[t], NULL);
+    fn(&jobs[0]);
+    for (int t = 1; t < n_threads; ++t)
+        if (ok[t]) pthread_join(th[t], NULL);
+}
+
+/*
+ * models.py:24-45 up to the LayerNorm statistics: per item, gather + pool each
+ * slot (fp32 in bag order, one round to the table dtype; models.py:27-33),
+ * concatenate into pooled[i, S*512] (fp32 values of the row dtype; models.py:43)
+ * and take the row's LayerNorm mean and fl(var + eps) in ATen CUDA's order.
+ */
+void rbo_rep_pool_stats(const void* table, int table_dtype, int64_t num_rows,
+                        const int64_t* const* values, const int64_t* const* offsets, const int64_t* nnz,
+                        int64_t n_slots, int64_t n_items, float eps, float* pooled, float* mean,
+                        float* var_eps, int n_threads) {
+    rep_job jb;
+    memset(&jb, 0, sizeof(jb));
+    jb.table = table; jb.table_dtype = table_dtype; jb.num_rows = num_rows;
+    jb.values = values; jb.offsets = offsets; jb.nnz = nnz;
+    jb.n_slots = n_slots; jb.n_items = n_items; jb.eps = eps;
+    jb.pooled = pooled; jb.mean = mean; jb.var_eps = var_eps;
+    run_jobs(jb, n_threads, pool_stats_worker);
+}
+
+/*
+ * models.py:45 + w8a8_linear's quantiser: LayerNorm of the pooled rows with the
+ * given mean and rstd (y rounded to the row dtype), then dynamic (act_mode 0)
+ * or static (act_mode 1) int8 quantisation; ln_out (optional) receives y.
+ */
+void rbo_rep_finish(const float* pooled, int row_dtype, int64_t n_slots, int64_t n_items, const float* mean,
+                    const float* rstd, const float* gamma, const float* beta, int act_mode, float static_scale,
+                    int8_t* q, float* scale, float* ln_out, int n_threads) {
+    rep_job jb;
+    memset(&jb, 0, sizeof(jb));
+    jb.table_dtype = row_dtype; jb.n_slots = n_slots; jb.n_items = n_items;
+    jb.pooled = (float*)pooled; jb.mean = (float*)mean; jb.rstd = rstd;
+    jb.gamma = gamma; jb.beta = beta; jb.act_mode = act_mode; jb.static_scale = static_scale;
+    jb.q = q; jb.scale = scale; jb.ln_out = ln_out;
+    run_jobs(jb, n_threads, finish_worker);
 }

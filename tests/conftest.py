@@ -39,6 +39,16 @@ def golden_rep(name):
     return dt, z["table"], batch, gamma, beta, float(z["eps"][0]), z
 
 
+def gpu_rsqrt(v):
+    """CUDA's rsqrtf of fp32 values, evaluated on the GPU (torch.rsqrt): the
+    function that gives rstd in ATen's CUDA LayerNorm and in K1.  GPU tests hand
+    it to the oracle, which cannot evaluate the hardware approximation itself."""
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32)).to("cuda")
+    return torch.rsqrt(t).cpu().numpy()
+
+
 @pytest.fixture(scope="session")
 def cuda_device():
     torch = pytest.importorskip("torch")

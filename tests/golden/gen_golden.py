@@ -1,9 +1,9 @@
 """Generate the golden fixtures in tests/golden/ from the reference itself.
 
-Run in a container that has the reference checked out (read-only) at
-/root/reference:
+Run where the reference is checked out (read-only), naming its directory:
 
-    TRITON_INTERPRET=1 python tests/golden/gen_golden.py
+    TRITON_INTERPRET=1 python tests/golden/gen_golden.py REFERENCE_DIR
+    (or set RB_REFERENCE_DIR instead of passing the argument)
 
 It imports the reference's own modules (models.RepEncoder, the W8A8 Triton
 kernels, the v1 quantisation kernels) and runs them on CPU:
@@ -32,7 +32,9 @@ os.environ.setdefault("TRITON_INTERPRET", "1")
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("RB_REFERENCE_DIR", "")
+if not REF or not os.path.isdir(REF):
+    sys.exit("usage: gen_golden.py REFERENCE_DIR (or RB_REFERENCE_DIR): the reference checkout to import")
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REF)

@@ -114,3 +114,28 @@ def test_ipc_entry_points_reject_null_arguments():
     ptr = ctypes.c_void_p(0)
     assert lib.rb_ipc_import(None, 0, ctypes.byref(ptr)) == _lib.RB_ERR_VALUE
     assert lib.rb_ipc_close(None, 0) == _lib.RB_ERR_VALUE
+
+
+def test_table_row_count_above_int32_is_rejected():
+    """Ids are clamped to [0, num_rows - 1] in 32 bits on the device, so every
+    gather entry point refuses num_rows >= 2^31 on the host (a caller passing
+    the table's element count instead of its rows would otherwise read outside
+    the table).  The pointers are never dereferenced: each call fails the host
+    check before any launch."""
+    from baidu_cti_grab_b200 import _lib
+
+    lib = _lib.load()
+    fake = 1 << 20
+    S, N = 2, 10
+    vals, offs = _lib.ptr_array([fake, fake]), _lib.ptr_array([fake, fake])
+    nnz, cols = _lib.i64_array([5, 5]), _lib.i32_array([0, 1])
+    too_many = 1 << 31
+    rc = lib.rb_rep_gather_ln_quant(fake, _lib.RB_BF16, too_many, 512, vals, offs, nnz, S, N, fake, fake,
+                                    _lib.RB_BF16, 1e-5, 0, None, 0, fake, S * 512, fake, None, None, None)
+    assert rc == _lib.RB_ERR_VALUE and "num_rows" in _lib.last_error()
+    rc = lib.rb_rep_gather_pool(fake, _lib.RB_BF16, too_many, 512, vals, offs, nnz, cols, S, N, fake, S * 512,
+                                None)
+    assert rc == _lib.RB_ERR_VALUE and "num_rows" in _lib.last_error()
+    rc = lib.rb_rep_gather_pool_scatter(fake, _lib.RB_BF16, too_many, 512, vals, offs, nnz, cols, S, N,
+                                        _lib.ptr_array([fake]), _lib.i64_array([0, N]), 1, S * 512, 0, None)
+    assert rc == _lib.RB_ERR_VALUE and "num_rows" in _lib.last_error()

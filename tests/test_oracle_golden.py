@@ -2,9 +2,14 @@
 
 tests/golden/gen_golden.py ran the reference's RepEncoder (ATen CPU) and its
 Triton kernels (interpreter) on these inputs.  The oracle must reproduce:
-pooled rows, every quantiser and the int8 GEMM + scaled epilogue bit for bit;
-its canonical-order LayerNorm may differ from ATen's by one bf16 ulp on a
-handful of elements, and the end-to-end int8 by one step there.
+pooled rows, every quantiser and the int8 GEMM + scaled epilogue bit for bit.
+
+The oracle's LayerNorm follows ATen's CUDA kernel, the one the reference runs
+on the GPU; tests/golden/gen_golden_aten_cuda.py recorded that kernel on a
+B200 (ln_aten_cuda.npz) and the oracle must reproduce its mean, rstd and
+output rows bit for bit.  ATen's CPU LayerNorm reduces in another order, so
+against the CPU-recorded RepEncoder fixtures the LayerNorm rows may differ by
+one bf16 ulp on a few elements and the end-to-end int8 by one step there.
 """
 
 import numpy as np
@@ -27,7 +32,7 @@ def test_rep_pooled_and_quantisers(name):
     q1, s1 = O.quant_rows_v1(lref)
     assert np.array_equal(q1, z["q_v1_ref"]) and np.array_equal(s1, z["scale_v1_ref"])
     assert np.array_equal(O.quant_static_v2(lref, z["static_scale"][0]), z["q_static_ref"])
-    # LayerNorm: canonical order vs ATen -- bf16 rows agree except for rare 1-ulp ties
+    # LayerNorm: ATen CUDA's order vs ATen CPU's -- bf16 rows agree except for rare 1-ulp ties
     if dt == "bfloat16":
         diff = ln != lref
         assert diff.mean() < 1e-3
@@ -89,3 +94,53 @@ def test_oracle_planted_error_is_caught():
     bad[row, 3] ^= 1
     _, _, pooled, _ = O.rep_forward(bad, dt, batch, gamma, beta, eps, intermediates=True)
     assert not np.array_equal(pooled, O.bf16_bits_to_f32(z["pooled_ref"]))
+
+
+def _aten_cuda_cases():
+    z = load_golden("ln_aten_cuda.npz")
+    return z, [str(c) for c in z["cases"]]
+
+
+@pytest.mark.parametrize("case", _aten_cuda_cases()[1])
+def test_layernorm_matches_aten_cuda(case):
+    """Mean, rstd and every LayerNorm output element equal ATen's CUDA kernel.
+    rstd = rsqrtf(var + eps) is the GPU's approximation: the fixture carries its
+    values on a window of fp32 arguments, in which the oracle's own
+    fl(var + eps) must be found and must give ATen's rstd."""
+    z, _ = _aten_cuda_cases()
+    bf = str(z[f"{case}_dtype"]) == "bf16"
+    tof = O.bf16_bits_to_f32 if bf else (lambda a: a.astype(np.float32))
+    x, g, b = tof(z[f"{case}_x"]), tof(z[f"{case}_gamma"]), tof(z[f"{case}_beta"])
+    eps = float(z["eps"][0])
+    args, vals = z[f"{case}_rsqrt_arg"], z[f"{case}_rsqrt_val"]
+
+    def rsqrt(v):
+        out = np.empty_like(v)
+        for r in range(len(v)):
+            hit = np.nonzero(args[r] == v[r])[0]
+            assert hit.size == 1, f"row {r}: fl(var + eps) = {v[r]!r} outside the recorded window"
+            out[r] = vals[r, hit[0]]
+        return out
+
+    y, mean, rstd = O.layernorm_rows(x, g, b, eps, "bfloat16" if bf else "float32", rsqrt=rsqrt)
+    assert np.array_equal(mean, z[f"{case}_mean"])
+    assert np.array_equal(rstd, z[f"{case}_rstd"])
+    assert np.array_equal(y.view(np.uint32), tof(z[f"{case}_y"]).view(np.uint32))
+    # the CPU-only default (correctly rounded 1/sqrt) is within 2 ulp of rsqrtf
+    _, _, r_cpu = O.layernorm_rows(x, g, b, eps, "float32")
+    assert np.abs(r_cpu.view(np.int32).astype(np.int64) - rstd.view(np.int32)).max() <= 2
+
+
+def test_layernorm_fixture_is_order_sensitive():
+    """The recorded means are not order-free: the correctly rounded mean (a
+    float64 sum) differs from ATen's on some rows, so reproducing the fixture
+    needs ATen's exact reduction order, not just an accurate one."""
+    z, cases = _aten_cuda_cases()
+    moved = 0
+    for case in cases:
+        bf = str(z[f"{case}_dtype"]) == "bf16"
+        x = (O.bf16_bits_to_f32 if bf else (lambda a: a.astype(np.float32)))(z[f"{case}_x"])
+        h = x.shape[1]
+        mean_other = (x.astype(np.float64).sum(axis=1) / h).astype(np.float32)
+        moved += int(np.sum(mean_other != z[f"{case}_mean"]))
+    assert moved > 0

@@ -1,6 +1,6 @@
 """rb_w8a8_gemm_noalloc: the GEMM entry point for callers that cannot allocate
-device memory (inside a graph capture they do not own, under another
-allocator's pool, or in hosts that forbid cudaMalloc after start-up).
+device memory (their memory belongs to another allocator's pool or a
+pre-sized arena, or their host forbids cudaMalloc after start-up).
 
 It is called here through the C ABI exactly as such a caller would, with only
 its inputs and outputs, and must reproduce the allocating entry point bit for
