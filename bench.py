@@ -19,11 +19,20 @@ activations (1.47 GB) are far larger than L2, so no L2 flush is needed.
 
 `e2e` runs the same batches through the public module API
 (RepEncoder.forward) from pinned host memory: one H2D copy of the packed ids
-and offsets and a D2H copy of the [N, 512] bf16 output inside the timed region.
+and offsets and a D2H copy of the [N, 512] bf16 output inside the timed region;
+`e2e.host_copy` times the same bytes with no kernels (the host-link ceiling).
+
+Also on the line (one GPU): `kernels.k1_uniform`, K1 on a batch whose ids are
+uniform over each slot's rows (no Zipf-hot rows in L2); `reference_gpu`, the
+reference's torch path on ATen's CUDA kernels for the same batch (W8A8 tail
+restated with ATen ops, and the bf16 Linear); `cpu_baseline`, the fp32
+64-user workload through the reference's arithmetic on all host cores, with
+the CPU model.
 
 `--impl reference` times the reference's algorithm on the host CPU cores
 (ATen embedding_bag / layer_norm + torch._int_mm, the oracle port in
-oracle/torch_ref.py) on a bounded sample of the same workload.
+oracle/torch_ref.py) on a bounded sample of the same workload, gathered from a
+full-size host table.
 """
 
 from __future__ import annotations
@@ -70,8 +79,10 @@ def parse_args(argv=None):
                          "of pooled rows (the 28 x 10M-row workload)")
     ap.add_argument("--gemm-sweep", action="store_true",
                     help="instead of the RepEncoder step: time K2 alone for M in 1..131072 (one JSON line per M)")
-    ap.add_argument("--cpu-sample-items", type=int, default=4096)
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ref-sample-items", type=int, default=2048,
+                    help="--impl reference: items of the batch each CPU step processes")
+    ap.add_argument("--no-reference-gpu", action="store_true")
+    ap.add_argument("--no-uniform-k1", action="store_true")
     return ap.parse_args(argv)
 
 
@@ -95,57 +106,99 @@ def profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples of one GPU while the timed region runs."""
+    """SM clock and throttle-reason samples of one GPU while the timed region
+    runs: NVML every 10 ms from a thread (nvidia-smi -lms 100 if NVML is
+    missing), so even a timed region of a few tens of ms gets several samples."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
+               ("sw_power_cap", 0x4))
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.thread = None
+        self.samples = []
         self.path = os.path.join("/tmp", f"rb_clocks_{os.getpid()}_{gpu_index}.csv")
+
+    def _nvml_loop(self, handle, nvml):
+        while not self.stop_flag:
+            try:
+                sm = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                mx = nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM)
+                rs = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                self.samples.append((float(sm), float(mx), int(rs)))
+            except Exception:  # noqa: BLE001 - sampling must never break the bench
+                pass
+            time.sleep(0.01)
 
     def start(self):
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", str(self.gpu)], stdout=self.f, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
-        time.sleep(0.3)
+            import threading
+
+            import pynvml as nvml
+
+            nvml.nvmlInit()
+            handle = nvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.stop_flag = False
+            self.thread = threading.Thread(target=self._nvml_loop, args=(handle, nvml), daemon=True)
+            self.thread.start()
+        except Exception:  # noqa: BLE001
+            self.thread = None
+            try:
+                self.f = open(self.path, "w")
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                     "-i", str(self.gpu)], stdout=self.f, stderr=subprocess.DEVNULL)
+            except (OSError, FileNotFoundError):
+                self.proc = None
+        time.sleep(0.05)
 
     def stop(self):
-        if self.proc is None:
-            return None
-        time.sleep(0.25)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.f.close()
         sm, smax, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    sm.append(float(parts[1]))
-                    smax = max(smax, float(parts[2]))
-                except ValueError:
-                    continue
-                for n, v in zip(names, parts[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(n)
-        os.unlink(self.path)
+        if self.thread is not None:
+            time.sleep(0.02)
+            self.stop_flag = True
+            self.thread.join(timeout=2)
+            for c, m, r in self.samples:
+                sm.append(c)
+                smax = max(smax, m)
+                for name, bit in self.REASONS:
+                    if r & bit:
+                        reasons.add(name)
+            source = "nvml 10 ms"
+        elif self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) < 9:
+                        continue
+                    try:
+                        sm.append(float(parts[1]))
+                        smax = max(smax, float(parts[2]))
+                    except ValueError:
+                        continue
+                    for n, v in zip(names, parts[5:9]):
+                        if v.lower() == "active":
+                            reasons.add(n)
+            os.unlink(self.path)
+            source = "nvidia-smi 100 ms"
+        else:
+            return None
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "sampler": source}
 
 
 def k1_bytes(n_items: int, nnz_total: int, elt: int = 2) -> int:
@@ -224,44 +277,64 @@ def time_graph_cycle(calls, reps: int = 5) -> float:
 
 
 # ------------------------------------------------------------- CPU baseline
-def cpu_sample(batch, n_items: int):
-    """First n_items items of a numpy batch, ids remapped onto a compact table of
-    the touched rows (row 0 = padding).  Returns (values, offsets, n_rows)."""
-    n = min(n_items, len(batch[1][1]) - 1)
-    vals, offs = [], []
-    for s in range(1, 29):
-        v, o = batch[s]
-        end = int(o[n])
-        vals.append(np.asarray(v[:end]))
-        offs.append(np.asarray(o[: n + 1]))
-    allv = np.concatenate(vals)
-    uniq, inv = np.unique(allv, return_inverse=True)
-    pos = 0
-    out_vals = []
-    for v in vals:
-        out_vals.append((inv[pos: pos + len(v)] + 1).astype(np.int64))
-        pos += len(v)
-    return out_vals, offs, len(uniq) + 1, n
+def cpu_model() -> str:
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for line in out.splitlines():
+            if line.lower().startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except (OSError, subprocess.SubprocessError):
+        pass
+    return "unknown"
 
 
-def run_cpu_reference(batch, n_items: int, seconds: float, steps: int = 0, warmup: int = 1):
-    """Time the torch-CPU restatement of the reference path; returns (items/s, info)."""
+def host_mem_available() -> int:
+    try:
+        return os.sysconf("SC_PAGE_SIZE") * os.sysconf("SC_AVPHYS_PAGES")
+    except (ValueError, OSError):
+        return 0
+
+
+def host_table(num_rows: int, dtype, seed: int, block_rows: int = 1 << 17):
+    """Host table [num_rows, 512] at full size: one seeded ~N(0, 0.02) block of
+    block_rows rows repeated (row 0 = padding).  The values only need realistic
+    magnitudes for timing; the full size is what makes the gather miss the host
+    caches as the real table does (a gathered compact table would not)."""
+    import torch
+
+    gen = torch.Generator().manual_seed(seed)
+    blk = (torch.randn((block_rows, 512), generator=gen) * 0.02).to(dtype)
+    t = torch.empty((num_rows, 512), dtype=dtype)
+    for r0 in range(0, num_rows, block_rows):
+        r1 = min(num_rows, r0 + block_rows)
+        t[r0:r1] = blk[: r1 - r0]
+    t[0] = 0
+    return t
+
+
+def cpu_weights(dtype, seed: int):
+    """LayerNorm default init (gamma 1, beta 0) and Linear(14336, 512) default init
+    quantised per output channel (the reference's weight prep restated in torch)."""
+    import torch
+
+    gen = torch.Generator().manual_seed(seed)
+    bound = 1.0 / H ** 0.5
+    w = (torch.rand((D_OUT, H), generator=gen) * 2 - 1) * bound
+    bias = ((torch.rand(D_OUT, generator=gen) * 2 - 1) * bound).to(dtype)
+    amax = w.abs().amax(dim=1).clamp(min=1e-8)
+    w_scale = amax / 127.0
+    w_nk = torch.round(w / w_scale[:, None]).clamp(-128, 127).to(torch.int8)
+    return torch.ones(H, dtype=dtype), torch.zeros(H, dtype=dtype), w_nk, w_scale, bias
+
+
+def time_cpu_forward(table, vals, offs, weights, n_items: int, warmup: int, steps: int):
+    """items/s of the torch-CPU restatement of the reference path over `steps` timed forwards."""
     import torch
     from oracle import torch_ref
 
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    vals, offs, n_rows, n = cpu_sample(batch, n_items)
-    gen = torch.Generator().manual_seed(0)
-    table = (torch.randn((n_rows, 512), generator=gen) * 0.02).to(torch.bfloat16)
-    table[0] = 0
-    gamma = (1 + 0.1 * torch.randn(H, generator=gen)).to(torch.bfloat16)
-    beta = (0.1 * torch.randn(H, generator=gen)).to(torch.bfloat16)
-    w_nk = torch.randint(-128, 128, (D_OUT, H), dtype=torch.int8, generator=gen)
-    w_scale = torch.rand(D_OUT, generator=gen) * 1e-2
-    bias = (0.02 * torch.randn(D_OUT, generator=gen)).to(torch.bfloat16)
-    tv = [torch.from_numpy(v) for v in vals]
-    to = [torch.from_numpy(o) for o in offs]
+    gamma, beta, w_nk, w_scale, bias = weights
+    tv = [torch.as_tensor(v) for v in vals]
+    to = [torch.as_tensor(o) for o in offs]
 
     def one():
         return torch_ref.rep_forward_cpu(table, tv, to, gamma, beta, 1e-5, w_nk, w_scale, bias)
@@ -269,36 +342,97 @@ def run_cpu_reference(batch, n_items: int, seconds: float, steps: int = 0, warmu
     for _ in range(max(1, warmup)):
         one()
     times = []
-    t_start = time.perf_counter()
-    while True:
+    for _ in range(max(1, steps)):
         t0 = time.perf_counter()
         one()
         times.append(time.perf_counter() - t0)
-        if steps > 0 and len(times) >= steps:
-            break
-        if steps <= 0 and (time.perf_counter() - t_start > seconds or len(times) >= 50):
-            break
-    total = sum(times)
-    info = {"cores": threads, "reps": len(times), "items_per_rep": n,
-            "sample": f"{n} items of the workload's first batch ({sum(len(v) for v in vals)} ids; "
-                      f"table rows gathered to a compact {n_rows}-row bf16 table), "
-                      f"{len(times)} timed forwards"}
-    return n * len(times) / total, info
+    return n_items * len(times) / sum(times), times
+
+
+def cpu_baseline_fp32(seconds_cap: float = 60.0):
+    """The CPU baseline of the benchmark plan: the fp32 workload of 64 users
+    (28 slots, 100k rows per slot ~N(0,0.02), sequence lengths U[1,64], ids
+    U[1,4] per item and slot, Zipf(1.1)), the whole batch, the full 5.7 GB fp32
+    table, through the reference's RepEncoder arithmetic (ATen CPU embedding_bag,
+    cat, layer_norm) and the dynamic W8A8 tail (quantiser, torch._int_mm, fp32
+    dequant); 3 warm-up and 10 timed forwards on all host cores."""
+    import torch
+    from baidu_cti_grab_b200 import synth
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = synth.CPU_FP32_SMALL
+    batch = synth.make_batch(cfg, seed=0)
+    n, nnz = synth.batch_stats(batch)
+    table = host_table(cfg.num_rows, torch.float32, seed=0)
+    weights = cpu_weights(torch.float32, seed=1)
+    vals = [batch[s][0] for s in range(1, 29)]
+    offs = [batch[s][1] for s in range(1, 29)]
+    value, times = time_cpu_forward(table, vals, offs, weights, n, warmup=3, steps=10)
+    del table
+    return {"value": round(value, 1), "unit": "items/s", "cores": threads, "kind": "port",
+            "cpu_model": cpu_model(),
+            "sample": f"the whole fp32 batch of {cfg.name} ({n} items, {nnz} ids, full {cfg.num_rows}-row "
+                      f"fp32 table), 3 warm-up + 10 timed forwards, {statistics.mean(times) * 1e3:.1f} ms each"}
 
 
 # --------------------------------------------------------------- main arms
+def workload_config(cfg, users: int, n_mean: float, nnz_mean: float, world: int) -> dict:
+    return {"workload": cfg.name, "users_per_gpu": users, "items_per_gpu_per_step": int(n_mean),
+            "ids_per_gpu_per_step": int(nnz_mean), "slots": 28, "emb_dim": 512,
+            "rows_per_slot": cfg.rows_per_slot,
+            "table": f"bf16 {cfg.num_rows * 1024 / 1e9:.1f} GB, one per GPU",
+            "linear": "14336->512 W8A8, per-channel weight scales, bf16 out",
+            "act_quant": "dynamic per-token int8", "zipf_a": cfg.zipf_a,
+            "l2": "inputs larger than L2 (28.7 GB table, 1.47 GB int8 activations); no flush",
+            "parallelism": f"dp{world} (users partitioned, no collective)"}
+
+
 def reference_arm(args):
+    """The reference's algorithm on the host cores (torch-CPU restatement of
+    models.py:24-48 + the W8A8 tail): each step is a bounded sample of the
+    benchmark step -- the first --ref-sample-items items of a 1024-user batch,
+    gathered from the full-size 28.7 GB bf16 table."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    import torch
     from baidu_cti_grab_b200 import synth
 
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
     cfg = synth.PROD_BF16_1M
-    batch = synth.make_batch(cfg, seed=1000, num_users=args.users)
-    n_items = min(args.cpu_sample_items, 2048)
-    per_step = []
-    # each step is one bounded sample forward; --warmup/--steps as given
-    value, info = run_cpu_reference(batch, n_items, seconds=0, steps=max(1, args.steps), warmup=args.warmup)
+    users = cfg.num_users if args.users is None else args.users
+    # the GPU arm's batches on rank 0 (seeds 1000, 1001, ... cycled over the
+    # steps), so that the config block -- mean items and ids per step -- is the same
+    batches = [synth.make_batch(cfg, seed=1000 + i, num_users=users) for i in range(args.batches)]
+    bstats = [synth.batch_stats(b) for b in batches]
+    K = max(1, args.steps)
+    n_all = sum(bstats[i % len(bstats)][0] for i in range(K)) / K
+    nnz_all = sum(bstats[i % len(bstats)][1] for i in range(K)) / K
+    batch = batches[0]
+    n = min(args.ref_sample_items, bstats[0][0])
+    vals = [batch[s][0][: int(batch[s][1][n])] for s in range(1, 29)]
+    offs = [batch[s][1][: n + 1] for s in range(1, 29)]
+    table_bytes = cfg.num_rows * 512 * 2
+    full = host_mem_available() > table_bytes + (16 << 30)
+    if full:
+        table = host_table(cfg.num_rows, torch.bfloat16, seed=0)
+        table_note = f"the full {cfg.num_rows}-row bf16 table ({table_bytes / 1e9:.1f} GB)"
+    else:  # not enough host memory for the full table: the touched rows, renumbered
+        allv = np.concatenate(vals)
+        uniq, inv = np.unique(allv, return_inverse=True)
+        pos, nv = 0, []
+        for v in vals:
+            nv.append((inv[pos: pos + len(v)] + 1).astype(np.int64))
+            pos += len(v)
+        vals = nv
+        table = host_table(len(uniq) + 1, torch.bfloat16, seed=0)
+        table_note = f"a compact {len(uniq) + 1}-row bf16 table of the touched rows (host memory below the full table)"
+    weights = cpu_weights(torch.bfloat16, seed=1)
+    value, times = time_cpu_forward(table, vals, offs, weights, n, warmup=args.warmup, steps=args.steps)
+    sample = (f"{n} items of a {users}-user batch ({sum(len(v) for v in vals)} ids) from {table_note}, "
+              f"{len(times)} timed forwards after {args.warmup} warm-up")
     line = {
         "impl": "reference",
         "metric": "RepEncoder items/s",
@@ -307,22 +441,48 @@ def reference_arm(args):
         "n_gpus": args.gpus,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(info["items_per_rep"] / value * 1e3, 3),
+        "ms_per_step": round(statistics.mean(times) * 1e3, 3),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "int8",
         "data": "synthetic",
-        "config": {"workload": cfg.name, "users_per_gpu": cfg.num_users if args.users is None else args.users,
-                   "slots": 28, "emb_dim": 512, "rows_per_slot": cfg.rows_per_slot, "linear": "14336->512 W8A8",
-                   "act_quant": "dynamic per-token", "parallelism": "host CPU, rank 0 only"},
-        "cpu_baseline": {"value": round(value, 1), "unit": "items/s", "cores": info["cores"], "kind": "port",
-                         "sample": info["sample"]},
+        "config": workload_config(cfg, users, n_all, nnz_all, args.gpus),
+        "cpu_baseline": {"value": round(value, 1), "unit": "items/s", "cores": threads, "kind": "port",
+                         "cpu_model": cpu_model(), "sample": sample},
         "e2e": {"value": round(value, 1), "unit": "items/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    del per_step
     print(json.dumps(line), flush=True)
     return 0
+
+
+def reference_gpu_forward(table, vals, offs, gamma, beta, eps, w_nk, w_scale, bias, w_bf16):
+    """The reference's torch path on the GPU with ATen's CUDA kernels
+    (models.py:27-47, fuse mode "torch": 28 x clamp + embedding_bag, cat,
+    layer_norm) followed by (a) its W8A8 tail restated with ATen ops -- dynamic
+    per-token quantiser (w8a8_triton_kernels.py:56-64), int8 GEMM
+    (torch._int_mm), ((acc*sa)*sb)+bias -- and (b) the unquantised bf16 Linear.
+    The reference's Triton kernels themselves cannot run where this bench runs."""
+    import torch
+    import torch.nn.functional as F
+
+    V = table.shape[0]
+    x = torch.cat([F.embedding_bag(v.clamp(0, V - 1), table, o[:-1], mode="sum", padding_idx=0)
+                   for v, o in zip(vals, offs)], dim=1)
+    y = F.layer_norm(x, (x.shape[1],), gamma, beta, eps)
+
+    def w8a8():
+        yf = y.float()
+        amax = yf.abs().amax(dim=1).clamp(min=1e-8)
+        t = yf * (127.0 / amax)[:, None]
+        q = (torch.sign(t) * torch.floor(t.abs() + 0.5)).clamp(-128, 127).to(torch.int8)
+        acc = torch._int_mm(q, w_nk.t())
+        return ((acc.float() * (amax / 127.0)[:, None]) * w_scale[None, :] + bias.float()).to(table.dtype)
+
+    def bf16_linear():
+        return F.linear(y, w_bf16, bias)
+
+    return w8a8, bf16_linear
 
 
 def b200_arm(args):
@@ -442,6 +602,51 @@ def b200_arm(args):
     sq_tops = 2 * 8192 ** 3 / (sq_ms * 1e-3) / 1e12
     del sq
 
+    # ---- K1 on uniformly drawn ids (no Zipf-hot rows, so no L2 reuse to help the
+    # gather): the control case for K1's HBM fraction (rank 0, one GPU)
+    k1_uniform = None
+    if world == 1 and not args.no_uniform_k1 and not args.uniform_ids:
+        import dataclasses
+        ucfg = dataclasses.replace(cfg, zipf_a=0.0, name=cfg.name + "-uniform-ids")
+        ub = synth.make_batch(ucfg, seed=2000, num_users=users)
+        uv = [torch.from_numpy(ub[s][0]).to(dev) for s in range(1, 29)]
+        uo = [torch.from_numpy(ub[s][1]).to(dev) for s in range(1, 29)]
+        un, unnz = synth.batch_stats(ub)
+        uq = q_buf[:un] if un <= n_items_max else torch.empty((un, H), dtype=torch.int8, device=dev)
+        us = s_buf[:un] if un <= n_items_max else torch.empty((un,), dtype=torch.float32, device=dev)
+        u_ms = time_cuda(lambda: device_ops.rep_gather_ln_quant(table, uv, uo, gamma, beta, 1e-5,
+                                                                 q_out=uq, scale_out=us), reps=5)
+        ub_bytes = k1_bytes(un, unnz)
+        k1_uniform = {"avg_ms": round(u_ms, 4), "items": un, "ids": unnz, "algorithmic_bytes": ub_bytes,
+                      "achieved": round(ub_bytes / (u_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                      "what": "K1 on a batch of the same shape with ids uniform over each slot's 1M rows"}
+        del uv, uo, uq, us
+
+    # ---- the reference's own torch path on this GPU (ATen CUDA kernels): the
+    # GPU bar of the benchmark plan (rank 0, one GPU, the first batch)
+    reference_gpu = None
+    if world == 1 and not args.no_reference_gpu:
+        vals0, offs0 = dev_batches[0]
+        with torch.no_grad():
+            w8a8_fn, bf16_fn = reference_gpu_forward(table, vals0, offs0, gamma, beta, 1e-5, w_nk, w_scale, bias,
+                                                     w.to(bf))
+            pre_ms = time_cuda(lambda: reference_gpu_forward(table, vals0, offs0, gamma, beta, 1e-5, w_nk,
+                                                             w_scale, bias, w.to(bf)), reps=3, warmup=1)
+            w8_ms = time_cuda(w8a8_fn, reps=3, warmup=1)
+            lin_ms = time_cuda(bf16_fn, reps=3, warmup=1)
+        n0 = stats[0][0]
+        reference_gpu = {
+            "w8a8_dynamic": {"value": round(n0 / ((pre_ms + w8_ms) * 1e-3), 1), "unit": "items/s",
+                             "ms": round(pre_ms + w8_ms, 4)},
+            "bf16_linear": {"value": round(n0 / ((pre_ms + lin_ms) * 1e-3), 1), "unit": "items/s",
+                            "ms": round(pre_ms + lin_ms, 4)},
+            "what": "the reference's torch RepEncoder on ATen CUDA (28 x clamp + embedding_bag, cat, layer_norm; "
+                    f"{pre_ms:.3f} ms) plus its dynamic W8A8 tail restated with ATen ops and torch._int_mm, or "
+                    "plus the bf16 nn.Linear (cuBLAS); same batch, same GPU; the reference's Triton kernels "
+                    "cannot run here"}
+        del w8a8_fn, bf16_fn
+        torch.cuda.empty_cache()
+
     # ---- e2e through the public API from pinned host memory: packed host
     # batches, H2D / forward / D2H of successive batches overlapped on streams
     e2e = None
@@ -469,14 +674,38 @@ def b200_arm(args):
         e_items = sum(pb.num_items for pb in seq)
         e2e = [e_items, e_ms, sum(pb.nbytes for pb in seq) / K, sum(pb.num_items * D_OUT * 2 for pb in seq) / K,
                chunk_items, str(seq[0].host.dtype).replace("torch.", ""), args.e2e_tail_parts]
+        # the same bytes with no kernels: each step's packed ids H2D and its
+        # bf16 rows D2H on two streams at once, K steps; the host-link ceiling
+        # the e2e figure runs against (all ranks at once when N > 1)
+        s_h2d, s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
+        dev_in = torch.empty((max(pb.host.numel() for pb in packed),), dtype=packed[0].host.dtype, device=dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(s_h2d)
+        s_d2h.wait_event(c0)
+        for i in range(K):
+            pb, ho = seq[i], outs[i]
+            with torch.cuda.stream(s_h2d):
+                dev_in[: pb.host.numel()].copy_(pb.host, non_blocking=True)
+            with torch.cuda.stream(s_d2h):
+                ho.copy_(out_buf[: ho.shape[0]], non_blocking=True)
+        s_h2d.wait_stream(s_d2h)
+        c1.record(s_h2d)
+        torch.cuda.synchronize()
+        copy_ms = c0.elapsed_time(c1)
+        e2e.append(copy_ms)
+        del dev_in
 
     # ---- max over ranks
-    vals = torch.tensor([ms, e2e[1] if e2e else 0.0, k1_ms, k2_ms], dtype=torch.float64, device=dev)
+    vals = torch.tensor([ms, e2e[1] if e2e else 0.0, k1_ms, k2_ms, e2e[7] if e2e else 0.0], dtype=torch.float64,
+                        device=dev)
     cnt = torch.tensor([items, e2e[0] if e2e else 0, nnz_timed], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
         dist.all_reduce(cnt, op=dist.ReduceOp.SUM)
-    ms_max, e2e_ms_max, k1_ms_max, k2_ms_max = [float(x) for x in vals.tolist()]
+    ms_max, e2e_ms_max, k1_ms_max, k2_ms_max, copy_ms_max = [float(x) for x in vals.tolist()]
     items_all, e2e_items_all, nnz_all = [float(x) for x in cnt.tolist()]
 
     line = None
@@ -522,14 +751,7 @@ def b200_arm(args):
             "vs_baseline": None,
             "dtype": "int8",
             "data": "synthetic",
-            "config": {"workload": cfg.name, "users_per_gpu": users, "items_per_gpu_per_step": int(n_mean),
-                       "ids_per_gpu_per_step": int(nnz_mean), "slots": 28, "emb_dim": 512,
-                       "rows_per_slot": cfg.rows_per_slot,
-                       "table": f"bf16 {cfg.num_rows * 1024 / 1e9:.1f} GB, one per GPU",
-                       "linear": "14336->512 W8A8, per-channel weight scales, bf16 out",
-                       "act_quant": "dynamic per-token int8", "zipf_a": cfg.zipf_a,
-                       "l2": "inputs larger than L2 (28.7 GB table, 1.47 GB int8 activations); no flush",
-                       "parallelism": f"dp{world} (users partitioned, no collective)"},
+            "config": workload_config(cfg, users, n_mean, nnz_mean, world),
             "roofline": dominant,
             "kernels": {"k1": roof_k1, "k2": roof_k2},
             "gpu_launches": 2 * K,
@@ -543,6 +765,17 @@ def b200_arm(args):
                                   "items one pinned H2D copy of its packed ids/offsets (int32 when they fit), "
                                   "K1 + K2, and one D2H copy of its bf16 output rows; copies of one chunk overlap "
                                   "the kernels of the next"}
+            copy_bytes = (e2e[2] + e2e[3]) * K * world
+            line["e2e"]["host_copy"] = {
+                "gbs": round(copy_bytes / (copy_ms_max * 1e-3) / 1e9, 1), "ms_per_step": round(copy_ms_max / K, 4),
+                "items_per_s_ceiling": round(items_all / (copy_ms_max * 1e-3), 1),
+                "what": "the e2e steps' H2D and D2H bytes alone (two streams, no kernels), all ranks at once: "
+                        "the host-link ceiling of the e2e figure"}
+        if k1_uniform is not None:
+            k1_uniform["frac"] = round(k1_uniform["achieved"] / hbm_peak, 4)
+            line["kernels"]["k1_uniform"] = k1_uniform
+        if reference_gpu is not None:
+            line["reference_gpu"] = reference_gpu
 
     # ---- CPU baseline (rank 0, N=1 only)
     if world > 1:
@@ -550,9 +783,7 @@ def b200_arm(args):
         dist.destroy_process_group()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            v, info = run_cpu_reference(host_batches[0], args.cpu_sample_items, args.cpu_seconds)
-            line["cpu_baseline"] = {"value": round(v, 1), "unit": "items/s", "cores": info["cores"],
-                                    "kind": "port", "sample": info["sample"]}
+            line["cpu_baseline"] = cpu_baseline_fp32()
         print(json.dumps(line), flush=True)
     return 0
 
