@@ -48,6 +48,19 @@
 #ifndef RB_GEMM_PAIR_MIN_M
 #define RB_GEMM_PAIR_MIN_M 4096
 #endif
+// M range of the swapped-operand cluster kernel (the weight as the MMA's 128-row
+// operand, the activation rows as its N, K split over a 16-CTA cluster).  Its
+// fixed cost (cluster launch, TMEM, two cluster barriers, the DSMEM sum) is
+// about 3.9 us on a B200, so the dp4a GEMV keeps M <= RB_GEMV_MAX_M, and above
+// 128 rows the split one-SM kernel is faster again (K = 14336, N = 512:
+// M = 17 / 64 / 128 take 8.4 / 9.5 / 12.3 us against 10.8 / 12.0 / 14.5 us
+// split; M = 256 16.5 against 15.1 us).
+#ifndef RB_GEMV_MAX_M
+#define RB_GEMV_MAX_M 16
+#endif
+#ifndef RB_GEMM_SWAP_MAX_M
+#define RB_GEMM_SWAP_MAX_M 128
+#endif
 
 namespace rb {
 namespace tc {
@@ -506,17 +519,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // fetches its own halves; the leader's full barrier counts both CTAs' bytes.
 namespace pair {
 constexpr int BM = 256;  // rows per tile (128 per CTA)
-constexpr int BN = 256;
 constexpr int BK = 128;  // K bytes per stage
-constexpr int STAGES = 6;
 constexpr int A_BYTES = 128 * BK;  // this CTA's A half
-constexpr int B_BYTES = 128 * BK;  // this CTA's B half
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TMEM_COLS = 512;
 constexpr int NUM_THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
-constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
+// Tile width BN = 256 (the default) or 128 (when the 256-wide tiles leave
+// pairs idle: at M = 4096, N = 512 there are 32 of them for 74 pairs).  Each
+// CTA loads BN / 2 rows of B per stage; the ring takes up to 192 KB.
+template <int kBN>
+struct Cfg {
+  static constexpr int BN = kBN;
+  static constexpr int B_BYTES = (kBN / 2) * BK;  // this CTA's B half
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * kBN;  // two accumulators
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                                    ((uint32_t)(BM >> 4) << 24);
+};
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -540,12 +559,13 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1), "l"(policy)
       : "memory");
 }
-__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
       "r"(0u));
 }
 // arrive on the barrier at this shared offset in both CTAs of the pair when the MMAs issued so far are done
@@ -559,9 +579,16 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+template <int kBN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     w8a8_gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const __grid_constant__ EpiParams ep) {
+  using C = Cfg<kBN>;
+  constexpr int BN = C::BN;
+  constexpr int B_BYTES = C::B_BYTES;
+  constexpr int STAGE_BYTES = C::STAGE_BYTES;
+  constexpr int STAGES = C::STAGES;
+  constexpr int TMEM_COLS = C::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
@@ -626,7 +653,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int64_t tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
         const int m0 = (int)((tile / n_tiles) * BM) + (int)rank * 128;
-        const int n0 = (int)((tile % n_tiles) * BN) + (int)rank * 128;
+        const int n0 = (int)((tile % n_tiles) * BN) + (int)rank * (BN / 2);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, kWaitTimeoutProducer, abort_flag)) {
             ok = false;
@@ -672,7 +699,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint64_t bdesc = sw128_desc(smem_u32(sB + stage * B_BYTES));
 #pragma unroll
           for (int k = 0; k < BK / MMA_K; ++k)
-            umma_i8_pair(d_tmem, adesc + (uint64_t)(k * MMA_K / 16), bdesc + (uint64_t)(k * MMA_K / 16),
+            umma_i8_pair(d_tmem, adesc + (uint64_t)(k * MMA_K / 16), bdesc + (uint64_t)(k * MMA_K / 16), C::IDESC,
                          (kb > 0 || k > 0) ? 1u : 0u);
           umma_commit_both(smem_u32(&empty[stage]));
           if (++stage == STAGES) {
@@ -963,6 +990,252 @@ __global__ void __launch_bounds__(kGvThreads * gv_groups(MT), gv_groups(MT) > 1 
   }
 }
 
+// ----------------------------------------------------------------------------
+// Small M (1 <= M <= kSwapMaxM): the operands swapped and K split over a
+// cluster.  Out^T = W * A^T: the weight's 128-row tile is the MMA's M side
+// and the activation rows (padded to MP, a multiple of 16) its N side, so
+// one tcgen05.mma.kind::i8 (M = 128, N = MP, K = 32) covers every row of A.
+// A cluster of kSwapSplit CTAs owns 128 output columns; CTA r takes the r-th
+// share of the K blocks.  Each CTA accumulates its int32 partial in TMEM,
+// stages it in shared memory ([128 columns][MP rows], padded against bank
+// conflicts), and after a cluster barrier CTA r sums the 8 columns
+// [8r, 8r + 8) across the cluster's shared memories (distributed shared
+// memory, int32 addition: exact in any order) and runs the epilogue for them.
+// One launch, no workspace; the weight streams through all clusters' SMs at
+// once.  No TMA load carries a multicast.
+namespace swp {
+constexpr int kSplit = 16;         // CTAs per cluster, along K (non-portable cluster size)
+constexpr int BK = 128;            // K bytes per stage
+constexpr int kMaxStages = 16;
+constexpr int kMaxMP = 256;
+constexpr int W_BYTES = 128 * BK;  // weight rows of the tile
+constexpr int NUM_THREADS = 192;
+constexpr int kColsPerCta = 128 / kSplit;  // output columns each CTA reduces
+// shared memory: a ring of stages of 16 KB of weight + MP x 128 B of A (as many
+// as fit, so that for small M every K block of the CTA is requested at once),
+// reused for the partial [128][MP + 4] int32 after the main loop
+constexpr int kRing = 192 * 1024;
+constexpr int SMEM_BYTES = kRing + 1024 + 256;
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void umma_i8_n(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ uint4 ld_cluster_v4(uint32_t cluster_addr) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
+// one output element: ((f32(acc) * sa) * sb) + bias in the output dtype, or the raw int32
+__device__ __forceinline__ void store_one(const EpiParams& ep, int64_t m, int64_t n, int32_t acc) {
+  const int64_t o = m * ep.ldo + n;
+  if (ep.out_dtype == RB_I32) {
+    reinterpret_cast<int32_t*>(ep.out)[o] = acc;
+    return;
+  }
+  float v = __fmul_rn(__int2float_rn(acc), load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? m : 0));
+  v = __fmul_rn(v, load_as_f32(ep.sb, ep.sb_dtype, n));
+  if (ep.bias != nullptr) v = __fadd_rn(v, load_as_f32(ep.bias, ep.bias_dtype, n));
+  if (ep.out_dtype == RB_F32) {
+    reinterpret_cast<float*>(ep.out)[o] = v;
+  } else if (ep.out_dtype == RB_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(ep.out)[o] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<__half*>(ep.out)[o] = __float2half_rn(v);
+  }
+}
+
+// tmW: the weight [N, K] (128-row boxes); tmA: the activations [M, K] (MP-row boxes)
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    w8a8_gemm_swap_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
+                          const __grid_constant__ EpiParams ep, int mp) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const int a_bytes = mp * BK;
+  const int stage_bytes = W_BYTES + a_bytes;                // 1024-aligned: mp is a multiple of 16
+  const int kStages = min(kMaxStages, kRing / stage_bytes);  // 4 at mp = 256, 10 at mp = 16
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kRing);
+  uint64_t* full = bars;                // [kMaxStages]  TMA -> MMA
+  uint64_t* empty = bars + kMaxStages;  // [kMaxStages]  MMA -> TMA
+  uint64_t* tfull = empty + kMaxStages; // [1]           MMA -> epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* part = reinterpret_cast<int32_t*>(smem);  // after the main loop: [128][mp + 4]
+  const int ldp = mp + 4;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = pair::cluster_rank();
+  const int64_t n_tile0 = (int64_t)(blockIdx.x / kSplit) * 128;
+  const int kblocks = (int)((ep.K + BK - 1) / BK);
+  const int kb0 = (int)((int64_t)rank * kblocks / kSplit);
+  const int kb1 = (int)((int64_t)(rank + 1) * kblocks / kSplit);
+  const bool has_k = kb1 > kb0;
+  const uint32_t tmem_cols = mp <= 32 ? 32u : (mp <= 64 ? 64u : (mp <= 128 ? 128u : 256u));
+  const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(mp >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kStages; ++st) {
+      mbar_init(smem_u32(&full[st]), 1);
+      mbar_init(smem_u32(&empty[st]), 1);
+    }
+    mbar_init(smem_u32(tfull), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && has_k) {
+      // ---------------------------------------------------------- producer
+      const uint64_t pol = policy_evict_first();
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, issued_phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, kWaitTimeoutProducer, abort_flag)) break;
+        const uint32_t fb = smem_u32(&full[stage]);
+        uint8_t* sW = smem + stage * stage_bytes;
+        mbar_arrive_expect_tx(fb, (uint32_t)stage_bytes);
+        tma_load_2d(smem_u32(sW), &tmW, kb * BK, (int)n_tile0, fb, pol);
+        tma_load_2d(smem_u32(sW + W_BYTES), &tmA, kb * BK, 0, fb, pol);
+        issued |= 1u << stage;
+        issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      // never leave a bulk copy in flight behind an exiting CTA (or a reused ring)
+      for (int st = 0; st < kStages; ++st)
+        if (issued & (1u << st))
+          mbar_wait_bounded(smem_u32(&full[st]), (issued_phase >> st) & 1u, kWaitTimeoutProducer, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && has_k) {
+      // --------------------------------------------------------------- MMA
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_bounded(smem_u32(&full[stage]), phase, kWaitTimeoutMma, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint8_t* sW = smem + stage * stage_bytes;
+        const uint64_t wdesc = sw128_desc(smem_u32(sW));
+        const uint64_t adesc = sw128_desc(smem_u32(sW + W_BYTES));
+#pragma unroll
+        for (int k = 0; k < BK / MMA_K; ++k)
+          umma_i8_n(tmem_base, wdesc + (uint64_t)(k * MMA_K / 16), adesc + (uint64_t)(k * MMA_K / 16), idesc,
+                    (kb > kb0 || k > 0) ? 1u : 0u);
+        umma_commit(smem_u32(&empty[stage]));
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      // the partial is complete (and the ring idle) once tfull flips
+      umma_commit(smem_u32(tfull));
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // --------------------------------------- TMEM -> shared partial [128][mp]
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // TMEM lane = output column of the tile
+    bool ready = !has_k;
+    if (has_k) ready = mbar_wait_bounded(smem_u32(tfull), 0, kWaitTimeoutEpilogue, abort_flag) && !*abort_flag;
+    tc_fence_after();
+    int32_t* dst = part + row * ldp;
+    for (int c = 0; c < mp; c += 16) {
+      uint32_t r[16];
+      if (has_k && ready) {
+        tmem_ld16(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c, r);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) r[i] = 0u;  // no K share (or a failed wait): a zero partial
+      }
+#pragma unroll
+      for (int i = 0; i < 16; i += 4)
+        *reinterpret_cast<uint4*>(dst + c + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  pair::cluster_sync_all();  // every CTA's partial is in its shared memory
+
+  // ---- CTA `rank` sums columns [8 rank, 8 rank + 8) of the tile over the cluster
+  {
+    const int m4n = (int)((ep.M + 3) / 4);     // groups of 4 rows of A that exist
+    const int items = kColsPerCta * m4n;       // (column, 4 consecutive rows of A)
+    const uint32_t part_addr = smem_u32(part);
+    for (int it = threadIdx.x; it < items; it += NUM_THREADS) {
+      const int j = it / m4n;
+      const int m4 = (it % m4n) * 4;
+      const int col = (int)rank * kColsPerCta + j;
+      const uint32_t off = (uint32_t)((col * ldp + m4) * 4);
+      uint4 v[kSplit];
+#pragma unroll
+      for (int q = 0; q < kSplit; ++q) v[q] = ld_cluster_v4(pair::map_rank(part_addr + off, (uint32_t)q));
+      uint4 acc = v[0];
+#pragma unroll
+      for (int q = 1; q < kSplit; ++q) {
+        acc.x += v[q].x;
+        acc.y += v[q].y;
+        acc.z += v[q].z;
+        acc.w += v[q].w;
+      }
+      const int64_t n = n_tile0 + col;
+      if (n < ep.N) {
+        const uint32_t a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (m4 + i < ep.M) store_one(ep, m4 + i, n, (int32_t)a4[i]);
+      }
+    }
+  }
+  pair::cluster_sync_all();  // no CTA leaves while another still reads its partial
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols)
+                 : "memory");
+  }
+}
+}  // namespace swp
+
 // CUDA-core GEMM for shapes the tensor-map path cannot take (K % 16 != 0,
 // unaligned operands, K == 0).  One thread per output element.
 __global__ void w8a8_gemm_simple_kernel(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb,
@@ -1047,6 +1320,7 @@ static int make_tmap(CUtensorMap* tm, const void* base, int64_t inner, int64_t o
 static std::once_flag g_attr_once[64];
 static std::once_flag g_pair_attr_once[64];
 static std::once_flag g_fp_attr_once[64];
+static std::once_flag g_swap_attr_once[64];
 
 }  // namespace tc
 }  // namespace rb
@@ -1061,7 +1335,9 @@ using namespace rb;
 constexpr int64_t kMaxKSplits = 16;
 static int choose_ksplits(int64_t M, int64_t N, int64_t K) {
   using namespace rb::tc;
-  if (M >= RB_GEMM_PAIR_MIN_M || M <= tc::kGemvMaxM || K <= 0 || K % 16 != 0) return 1;
+  if (M >= RB_GEMM_PAIR_MIN_M || M <= tc::kGemvMaxM || M <= RB_GEMV_MAX_M || M <= RB_GEMM_SWAP_MAX_M || K <= 0 ||
+      K % 16 != 0)
+    return 1;
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int64_t kblocks = (K + BK - 1) / BK;
   int64_t s = std::min<int64_t>(sm_count() / std::max<int64_t>(tiles, 1), kblocks / 2);
@@ -1119,7 +1395,7 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
     w8a8_gemm_simple_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(A, lda, B, ldb, ep);
     return check_cuda(cudaGetLastError(), "w8a8_gemm_simple_kernel launch");
   }
-  if (M <= kGemvMaxM) {
+  if (M <= RB_GEMV_MAX_M && M <= kGemvMaxM) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(((N + kGvCols - 1) / kGvCols) * kGvSplit));
     cfg.blockDim = dim3(kGvThreads * (M > 8 ? gv_groups(16) : 1));
@@ -1144,25 +1420,70 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
   int dev = 0;
   cudaGetDevice(&dev);
   int rc;
+  if (M <= RB_GEMM_SWAP_MAX_M) {
+    // swapped operands, K split over a 16-CTA cluster, partials summed over DSMEM
+    const int mp = (int)((M + 15) / 16 * 16);
+    CUtensorMap tmW, tmAct;
+    rc = make_tmap(&tmW, B, K, N, ldb, swp::BK, 128);
+    if (rc) return rc;
+    rc = make_tmap(&tmAct, A, K, M, lda, swp::BK, (uint32_t)mp);
+    if (rc) return rc;
+    cudaError_t se = cudaSuccess;
+    std::call_once(g_swap_attr_once[dev & 63], [&] {
+      se = cudaFuncSetAttribute(swp::w8a8_gemm_swap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                swp::SMEM_BYTES);
+      if (se == cudaSuccess)
+        se = cudaFuncSetAttribute(swp::w8a8_gemm_swap_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    });
+    if (se != cudaSuccess) return check_cuda(se, "cudaFuncSetAttribute(w8a8_gemm_swap_kernel)");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(((N + 127) / 128) * swp::kSplit));
+    cfg.blockDim = dim3(swp::NUM_THREADS);
+    cfg.dynamicSmemBytes = swp::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = swp::kSplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, swp::w8a8_gemm_swap_kernel, tmW, tmAct, ep, mp),
+                      "w8a8_gemm_swap_kernel launch");
+  }
   if (M >= RB_GEMM_PAIR_MIN_M) {
-    // two-SM tiles: each CTA of a pair loads 128 rows of A and 128 of B
+    // two-SM tiles: each CTA of a pair loads 128 rows of A and BN/2 of B.  A
+    // 128-wide tile re-reads A twice as often and runs about 1.45x longer per
+    // output column than a 256-wide one (L2-bound: K = 14336, N = 512 on a
+    // B200), so the narrow tiles are used only when they save whole waves:
+    // M = 4096 takes 50.4 us with them, 57.4 us without; M = 32768 246 against 169
+    const int pairs_avail = sm_count() / 2;
+    const int64_t mt = (M + pair::BM - 1) / pair::BM;
+    const int64_t t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128);
+    const int64_t cost256 = 4 * ((t256 + pairs_avail - 1) / pairs_avail);  // in quarter-units of a 128-wide tile
+    const int64_t cost128 = 3 * ((t128 + pairs_avail - 1) / pairs_avail);
+    const bool narrow = cost128 < cost256;
+    const int bn = narrow ? 128 : 256;
     CUtensorMap tpA, tpB;
     rc = make_tmap(&tpA, A, K, M, lda, pair::BK, 128);
     if (rc) return rc;
-    rc = make_tmap(&tpB, B, K, N, ldb, pair::BK, 128);
+    rc = make_tmap(&tpB, B, K, N, ldb, pair::BK, (uint32_t)(bn / 2));
     if (rc) return rc;
     cudaError_t pe = cudaSuccess;
     std::call_once(g_pair_attr_once[dev & 63], [&] {
-      pe = cudaFuncSetAttribute(pair::w8a8_gemm_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                pair::SMEM_BYTES);
+      pe = cudaFuncSetAttribute(pair::w8a8_gemm_tc_pair_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                pair::Cfg<256>::SMEM_BYTES);
+      if (pe == cudaSuccess)
+        pe = cudaFuncSetAttribute(pair::w8a8_gemm_tc_pair_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  pair::Cfg<128>::SMEM_BYTES);
     });
     if (pe != cudaSuccess) return check_cuda(pe, "cudaFuncSetAttribute(w8a8_gemm_tc_pair_kernel)");
-    const int64_t ptiles = ((M + pair::BM - 1) / pair::BM) * ((N + pair::BN - 1) / pair::BN);
-    const int pairs = (int)std::min<int64_t>(ptiles, sm_count() / 2);
+    const int64_t ptiles = narrow ? t128 : t256;
+    const int pairs = (int)std::min<int64_t>(ptiles, pairs_avail);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
     cfg.blockDim = dim3(pair::NUM_THREADS);
-    cfg.dynamicSmemBytes = pair::SMEM_BYTES;
+    cfg.dynamicSmemBytes = narrow ? pair::Cfg<128>::SMEM_BYTES : pair::Cfg<256>::SMEM_BYTES;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1171,8 +1492,11 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return check_cuda(cudaLaunchKernelEx(&cfg, pair::w8a8_gemm_tc_pair_kernel, tpA, tpB, ep),
-                      "w8a8_gemm_tc_pair_kernel launch");
+    if (narrow)
+      return check_cuda(cudaLaunchKernelEx(&cfg, pair::w8a8_gemm_tc_pair_kernel<128>, tpA, tpB, ep),
+                        "w8a8_gemm_tc_pair_kernel<128> launch");
+    return check_cuda(cudaLaunchKernelEx(&cfg, pair::w8a8_gemm_tc_pair_kernel<256>, tpA, tpB, ep),
+                      "w8a8_gemm_tc_pair_kernel<256> launch");
   }
   // one-SM tiles, split along K when the (m, n) tiles alone cannot fill the GPU
   int ks = choose_ksplits(M, N, K);

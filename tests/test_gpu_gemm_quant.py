@@ -229,7 +229,7 @@ def test_gemm_small_m_equals_tensor_core_rows(cuda_device, M, N, out_name):
     assert torch.equal(acc.double(), a[:M].double() @ b.double().t())
 
 
-@pytest.mark.parametrize("M", [17, 256, 700])
+@pytest.mark.parametrize("M", [300, 700, 2048])
 def test_gemm_split_k_equals_unsplit(cuda_device, M):
     """The split-K path (workspace given) and the unsplit kernel (rb_w8a8_gemm) agree bit for bit."""
     import torch
