@@ -51,6 +51,8 @@ SIGNATURES = {
     "rb_w8a8_gemm_workspace_size": [_i64, _i64, _i64],
     "rb_w8a8_gemm_noalloc": [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp, _i32, _vp,
                              _i64, _i32, _vp],
+    "rb_w8a8_gemm_ln": [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp, _i32, _vp,
+                        _i64, _i32, _vp, _vp, _i32, _f32, _vp, _i64, _vp],
     "rb_fp_gemm": [_vp, _i32, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _vp, _i64, _i32, _vp],
     "rb_rep_gather_pool_scatter": [_vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _i64, _vp, _vp, _i32, _i64,
                                    _i64, _vp],

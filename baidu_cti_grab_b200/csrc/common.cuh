@@ -108,6 +108,11 @@ __device__ __forceinline__ float load_as_f32(const void* p, int dtype, int64_t i
 // ------------------------------------------------------------ f32x2 math
 // Blackwell packed fp32: one instruction performs two IEEE round-to-nearest
 // operations.  Lanes of a pair are independent, so results equal the scalar ops.
+// A multiply whose result feeds an add must use mul2v / add2v: a build of this
+// library turned a plain asm multiply-then-add into one rounding instead of
+// two.  The volatile forms keep both roundings; they are not used everywhere
+// because they also stop the compiler from scheduling around them (K1 ran 19 %
+// slower with every helper volatile, with bit-identical results).
 struct F2 {
   unsigned long long r;
 };
@@ -139,6 +144,16 @@ __device__ __forceinline__ F2 mul2(F2 a, F2 b) {
 __device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) {
   F2 d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.r) : "l"(a.r), "l"(b.r), "l"(c.r));
+  return d;
+}
+__device__ __forceinline__ F2 mul2v(F2 a, F2 b) {
+  F2 d;
+  asm volatile("mul.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
+  return d;
+}
+__device__ __forceinline__ F2 add2v(F2 a, F2 b) {
+  F2 d;
+  asm volatile("add.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
   return d;
 }
 __device__ __forceinline__ F2 addrz2(F2 a, F2 b) {

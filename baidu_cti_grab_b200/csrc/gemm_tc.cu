@@ -248,7 +248,7 @@ __device__ __forceinline__ void epilogue_32(const uint32_t* r, int64_t row, int6
     const F2 sa2 = f2(sa_v, sa_v);
 #pragma unroll
     for (int j = 0; j < 16; ++j)
-      v[j] = mul2(f2(__int2float_rn((int)r[2 * j]), __int2float_rn((int)r[2 * j + 1])), sa2);
+      v[j] = mul2v(f2(__int2float_rn((int)r[2 * j]), __int2float_rn((int)r[2 * j + 1])), sa2);
   }
   const size_t osz = ep.out_dtype == RB_F32 ? 4 : 2;
   const bool vec = ncol == 32 && (kF32Acc || aligned(ep.sb, 16)) && (ep.bias == nullptr || aligned(ep.bias, 16)) &&
@@ -260,12 +260,12 @@ __device__ __forceinline__ void epilogue_32(const uint32_t* r, int64_t row, int6
       if constexpr (!kF32Acc) {
         ld_param8(ep.sb, ep.sb_dtype, col0 + 8 * g, p);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v[4 * g + k] = mul2(v[4 * g + k], p[k]);
+        for (int k = 0; k < 4; ++k) v[4 * g + k] = mul2v(v[4 * g + k], p[k]);
       }
       if (ep.bias != nullptr) {
         ld_param8(ep.bias, ep.bias_dtype, col0 + 8 * g, p);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v[4 * g + k] = add2(v[4 * g + k], p[k]);
+        for (int k = 0; k < 4; ++k) v[4 * g + k] = add2v(v[4 * g + k], p[k]);
       }
     }
     if (ep.out_dtype == RB_F32) {
@@ -755,6 +755,370 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                  : "memory");
+  }
+}
+
+// ----------------------------------------------------------------------------
+// K2 with the transformer's first LayerNorm fused (models.py:216-217: layer 0
+// starts with residual = x; x = norm1[0](x), x being the RepEncoder output).
+// A CTA pair computes 256 x 512 tiles: a whole 512-wide output row sits in one
+// CTA's TMEM (two N = 256 MMAs per K step, all 512 columns, one accumulator),
+// so the epilogue thread that owns a row writes rep_emb, takes the row's
+// LayerNorm statistics in the order of ATen's CUDA LayerNorm for a 512-wide
+// row (128 Welford chains of 4 elements, a shuffle-down merge of each group of
+// 32 chains, then groups {0,2}, {1,3} and the two halves), and writes
+// norm1(rep_emb) from a second read of TMEM.  The main loop waits for the
+// epilogue between tiles (one accumulator), a few percent of the tile time.
+struct LnParams {
+  const void* gamma;
+  const void* beta;
+  int ln_dtype;
+  float eps;
+  void* out;      // norm1 output [M, 512], same dtype as rep_emb
+  int64_t ldo;
+};
+constexpr int LN_BN = 512;
+constexpr int LN_B_BYTES = 2 * 128 * BK;  // this CTA's two 128-row slices of B
+constexpr int LN_STAGE_BYTES = A_BYTES + LN_B_BYTES;
+constexpr int LN_STAGES = 4;
+constexpr int LN_SMEM_BYTES = LN_STAGES * LN_STAGE_BYTES + 1024 + 256;
+constexpr uint32_t LN_IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
+                              ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void welford_push1(float& mean, float& m2, float x, float r) {
+  const float delta = __fsub_rn(x, mean);
+  mean = __fmaf_rn(delta, r, mean);
+  m2 = __fmaf_rn(delta, __fsub_rn(x, mean), m2);
+}
+
+// 32 output values of one row (columns col0 .. col0+31) from the int32
+// accumulators: ((f32(acc) * sa) * sb) + bias, rounded to the output dtype
+// (v[] holds the rounded values widened back to fp32)
+__device__ __forceinline__ void ln_out_values(const uint32_t* r, int64_t col0, float sa_v, const EpiParams& ep,
+                                              float* v) {
+  const F2 sa2 = f2(sa_v, sa_v);
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    F2 sb[4], bi[4];
+    ld_param8(ep.sb, ep.sb_dtype, col0 + 8 * g, sb);
+    if (ep.bias != nullptr) ld_param8(ep.bias, ep.bias_dtype, col0 + 8 * g, bi);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = 8 * g + 2 * k;
+      F2 x = mul2v(mul2v(f2(__int2float_rn((int)r[j]), __int2float_rn((int)r[j + 1])), sa2), sb[k]);
+      if (ep.bias != nullptr) x = add2v(x, bi[k]);
+      float2 xv = un(x);
+      if (ep.out_dtype == RB_BF16) {
+        xv.x = round_bf16(xv.x);
+        xv.y = round_bf16(xv.y);
+      } else if (ep.out_dtype == RB_F16) {
+        xv.x = __half2float(__float2half_rn(xv.x));
+        xv.y = __half2float(__float2half_rn(xv.y));
+      }
+      v[j] = xv.x;
+      v[j + 1] = xv.y;
+    }
+  }
+}
+
+// store 32 fp32 values (already representable in dtype) at dst, 32-byte stores when aligned
+__device__ __forceinline__ void ln_store32(void* dst, int dtype, const float* v) {
+  if (dtype == RB_F32) {
+    float* d = reinterpret_cast<float*>(dst);
+    if (aligned(d, 32)) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint32_t w[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) w[k] = __float_as_uint(v[8 * g + k]);
+        stg_v8(d + 8 * g, w);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) d[k] = v[k];
+    }
+    return;
+  }
+  uint32_t w[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k)
+    w[k] = dtype == RB_BF16 ? pack_bf16x2(v[2 * k], v[2 * k + 1]) : pack_f16x2(v[2 * k], v[2 * k + 1]);
+  uint16_t* d = reinterpret_cast<uint16_t*>(dst);
+  if (aligned(d, 32)) {
+    stg_v8(d, w);
+    stg_v8(d + 16, w + 8);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      d[2 * k] = (uint16_t)(w[k] & 0xffffu);
+      d[2 * k + 1] = (uint16_t)(w[k] >> 16);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    w8a8_gemm_ln_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ EpiParams ep, const __grid_constant__ LnParams lp) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + LN_STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LN_STAGES * LN_STAGE_BYTES);
+  uint64_t* full = bars;                   // [LN_STAGES]  leader: TMA bytes of both CTAs -> MMA
+  uint64_t* empty = bars + LN_STAGES;      // [LN_STAGES]  both: MMA done with the slot -> TMA
+  uint64_t* tfull = bars + 2 * LN_STAGES;  // [1]          both: accumulator ready -> epilogue
+  uint64_t* tempty = tfull + 1;            // [1]          leader: both epilogues done -> MMA
+  uint64_t* done = tempty + 1;             // [1]          leader: all MMAs complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < LN_STAGES; ++st) {
+      mbar_init(smem_u32(&full[st]), 1);
+      mbar_init(smem_u32(&empty[st]), 1);
+    }
+    mbar_init(smem_u32(tfull), 1);
+    mbar_init(smem_u32(tempty), 2 * 4);  // one arrival per epilogue warp of both CTAs
+    mbar_init(smem_u32(done), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int64_t num_tiles = (ep.M + BM - 1) / BM;
+  const int kblocks = (int)((ep.K + BK - 1) / BK);
+  const int64_t pair_id = blockIdx.x >> 1;
+  const int64_t num_pairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      const uint64_t pol_a = policy_evict_first(), pol_b = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, issued_phase = 0;
+      bool ok = true;
+      for (int64_t tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+        const int m0 = (int)(tile * BM) + (int)rank * 128;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, kWaitTimeoutProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb_local = smem_u32(&full[stage]);
+          if (leader) mbar_arrive_expect_tx(fb_local, 2 * LN_STAGE_BYTES);
+          const uint32_t fb = map_rank(fb_local, 0);
+          uint8_t* b = sB + stage * LN_B_BYTES;
+          tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), &tmA, kb * BK, m0, fb, pol_a);
+          tma_load_2d_pair(smem_u32(b), &tmB, kb * BK, (int)rank * 128, fb, pol_b);
+          tma_load_2d_pair(smem_u32(b + 128 * BK), &tmB, kb * BK, 256 + (int)rank * 128, fb, pol_b);
+          issued |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == LN_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (leader) {
+        for (int st = 0; st < LN_STAGES; ++st)
+          if (issued & (1u << st))
+            mbar_wait_bounded(smem_u32(&full[st]), (issued_phase >> st) & 1u, kWaitTimeoutProducer, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // --------------------------------------------------------------- MMA
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int64_t tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+        if (!mbar_wait_bounded(smem_u32(tempty), acc_phase ^ 1, kWaitTimeoutMma, abort_flag)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&full[stage]), phase, kWaitTimeoutMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = sw128_desc(smem_u32(sA + stage * A_BYTES));
+          const uint64_t bdesc0 = sw128_desc(smem_u32(sB + stage * LN_B_BYTES));
+          const uint64_t bdesc1 = sw128_desc(smem_u32(sB + stage * LN_B_BYTES + 128 * BK));
+#pragma unroll
+          for (int k = 0; k < BK / MMA_K; ++k) {
+            const uint32_t accf = (kb > 0 || k > 0) ? 1u : 0u;
+            umma_i8_pair(tmem_base, adesc + (uint64_t)(k * MMA_K / 16), bdesc0 + (uint64_t)(k * MMA_K / 16),
+                         LN_IDESC, accf);
+            umma_i8_pair(tmem_base + 256, adesc + (uint64_t)(k * MMA_K / 16), bdesc1 + (uint64_t)(k * MMA_K / 16),
+                         LN_IDESC, accf);
+          }
+          umma_commit_both(smem_u32(&empty[stage]));
+          if (++stage == LN_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_both(smem_u32(tfull));
+        acc_phase ^= 1;
+      }
+      asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       smem_u32(done))
+                   : "memory");
+      mbar_wait_bounded(smem_u32(done), 0, kWaitTimeoutMma, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const uint32_t tempty_leader = map_rank(smem_u32(tempty), 0);
+    const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    uint32_t acc_phase = 0;
+    const bool bf_ln = lp.ln_dtype == RB_BF16;
+    for (int64_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
+      if (!mbar_wait_bounded(smem_u32(tfull), acc_phase, kWaitTimeoutEpilogue, abort_flag)) break;
+      tc_fence_after();
+      const int64_t row = tile * BM + (int64_t)rank * 128 + quarter * 32 + lane;
+      const bool live = row < ep.M;
+      const float sa_v = live ? load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? row : 0) : 0.0f;
+      uint8_t* out_row = reinterpret_cast<uint8_t*>(ep.out) + (live ? row : 0) * ep.ldo * dtype_size(ep.out_dtype);
+      // pass 1: rep_emb, and per 128-column group (an ATen warp of 32 chains of
+      // 4 columns) the merged Welford state
+      float gmean[4], gm2[4];
+#pragma unroll 1
+      for (int w = 0; w < 4; ++w) {
+        float cm[32], cq[32];  // chains 32w .. 32w+31 (columns 128w + 4j .. +3)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          float v[32];
+          tmem_ld32(lane_base + (uint32_t)(128 * w + 32 * c), r);
+          ln_out_values(r, 128 * w + 32 * c, sa_v, ep, v);
+          if (live) ln_store32(out_row + (int64_t)(128 * w + 32 * c) * dtype_size(ep.out_dtype), ep.out_dtype, v);
+#pragma unroll
+          for (int q = 0; q < 8; q += 2) {  // chains 8c + q, 8c + q + 1: columns 4q .. 4q+7 of this chunk
+            Welford2 st{f2(0.0f, 0.0f), f2(0.0f, 0.0f)};
+            welford_push2(st, f2(v[4 * q], v[4 * q + 4]), 1.0f);
+            welford_push2(st, f2(v[4 * q + 1], v[4 * q + 5]), 0.5f);
+            welford_push2(st, f2(v[4 * q + 2], v[4 * q + 6]), 1.0f / 3.0f);
+            welford_push2(st, f2(v[4 * q + 3], v[4 * q + 7]), 0.25f);
+            const float2 m = un(st.mean), q2 = un(st.m2);
+            cm[8 * c + q] = m.x;
+            cm[8 * c + q + 1] = m.y;
+            cq[8 * c + q] = q2.x;
+            cq[8 * c + q + 1] = q2.y;
+          }
+        }
+        // shuffle-down merge of the 32 chains: chain j takes chain j + d
+        float cnt = 4.0f;
+#pragma unroll
+        for (int d = 16; d >= 1; d >>= 1) {
+#pragma unroll
+          for (int j = 0; j < d; ++j) {
+            const float2 mq = welford_merge1(cm[j], cq[j], cm[j + d], cq[j + d], cnt);
+            cm[j] = mq.x;
+            cq[j] = mq.y;
+          }
+          cnt = __fadd_rn(cnt, cnt);
+        }
+        gmean[w] = cm[0];
+        gm2[w] = cq[0];
+      }
+      // the accumulator is no longer needed: let the MMA warp start the next tile
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty_leader);
+      // groups 0, 1 take groups 2, 3 (128 elements each), then 0 takes 1 (256 each)
+      const float2 g02 = welford_merge1(gmean[0], gm2[0], gmean[2], gm2[2], 128.0f);
+      const float2 g13 = welford_merge1(gmean[1], gm2[1], gmean[3], gm2[3], 128.0f);
+      const float2 fin = welford_merge1(g02.x, g02.y, g13.x, g13.y, 256.0f);
+      const float mean = fin.x;
+      const float rstd = rsqrtf(__fadd_rn(__fdiv_rn(fin.y, 512.0f), lp.eps));
+      // pass 2: norm1(rep_emb) = fma(gamma, rstd * (x - mean), beta), rounded to the
+      // dtype, from the row this thread stored in pass 1 (program order makes it visible)
+      uint8_t* ln_row = reinterpret_cast<uint8_t*>(lp.out) + (live ? row : 0) * lp.ldo * dtype_size(ep.out_dtype);
+      if (live) {
+#pragma unroll 1
+        for (int c = 0; c < LN_BN / 32; ++c) {
+          float v[32];
+          const uint8_t* src = out_row + (int64_t)(32 * c) * dtype_size(ep.out_dtype);
+          if (ep.out_dtype == RB_F32) {
+            const float4* q = reinterpret_cast<const float4*>(src);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const float4 t = q[k];
+              v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
+            }
+          } else {
+            const uint4* q = reinterpret_cast<const uint4*>(src);
+            const bool bf = ep.out_dtype == RB_BF16;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint4 t = q[k];
+              const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                if (bf) {
+                  v[8 * k + 2 * h] = bf16_lo(w[h]);
+                  v[8 * k + 2 * h + 1] = bf16_hi(w[h]);
+                } else {
+                  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[h]));
+                  v[8 * k + 2 * h] = f.x;
+                  v[8 * k + 2 * h + 1] = f.y;
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int gq = 0; gq < 4; ++gq) {
+            F2 gg[4], bb[4];
+            ld_param8(lp.gamma, lp.ln_dtype, 32 * c + 8 * gq, gg);
+            ld_param8(lp.beta, lp.ln_dtype, 32 * c + 8 * gq, bb);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 g2 = un(gg[k]), b2 = un(bb[k]);
+              const int j = 8 * gq + 2 * k;
+              v[j] = __fmaf_rn(g2.x, __fmul_rn(rstd, __fsub_rn(v[j], mean)), b2.x);
+              v[j + 1] = __fmaf_rn(g2.y, __fmul_rn(rstd, __fsub_rn(v[j + 1], mean)), b2.y);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            if (ep.out_dtype == RB_BF16) v[k] = round_bf16(v[k]);
+            else if (ep.out_dtype == RB_F16) v[k] = __half2float(__float2half_rn(v[k]));
+          }
+          ln_store32(ln_row + (int64_t)(32 * c) * dtype_size(ep.out_dtype), ep.out_dtype, v);
+        }
+      }
+      (void)bf_ln;
+      acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512) : "memory");
   }
 }
 }  // namespace pair
@@ -1321,6 +1685,7 @@ static std::once_flag g_attr_once[64];
 static std::once_flag g_pair_attr_once[64];
 static std::once_flag g_fp_attr_once[64];
 static std::once_flag g_swap_attr_once[64];
+static std::once_flag g_ln_attr_once[64];
 
 }  // namespace tc
 }  // namespace rb
@@ -1535,6 +1900,89 @@ extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64
                             void* stream) {
   return rb_w8a8_gemm_ws(A, lda, B, ldb, M, N, K, sa, sa_dtype, sa_per_row, sb, sb_dtype, bias, bias_dtype, out,
                          ldo, out_dtype, nullptr, 0, stream);
+}
+
+// ----------------------------------------------------------------------------
+// K2 + the transformer's layer-0 LayerNorm(512): out as rb_w8a8_gemm, and
+// ln_out = LayerNorm(out) with gamma/beta (ATen's CUDA order, bit for bit).
+extern "C" int rb_w8a8_gemm_ln(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M, int64_t N,
+                               int64_t K, const void* sa, int sa_dtype, int sa_per_row, const void* sb, int sb_dtype,
+                               const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
+                               const void* ln_gamma, const void* ln_beta, int ln_dtype, float eps, void* ln_out,
+                               int64_t ldl, void* stream) {
+  using namespace rb::tc;
+  if (M < 0 || K < 0) return fail(RB_ERR_VALUE, "negative GEMM shape");
+  if (N != pair::LN_BN) return fail(RB_ERR_UNSUPPORTED, "rb_w8a8_gemm_ln needs N == 512, got %lld", (long long)N);
+  if (M == 0) return RB_OK;
+  if (A == nullptr || B == nullptr || out == nullptr || ln_out == nullptr) return fail(RB_ERR_VALUE, "null operand");
+  if (lda < K || ldb < K || ldo < N || ldl < N) return fail(RB_ERR_VALUE, "leading dimension smaller than the row");
+  if (out_dtype != RB_BF16 && out_dtype != RB_F16 && out_dtype != RB_F32)
+    return fail(RB_ERR_VALUE, "out dtype must be bf16/f16/f32");
+  auto fdt = [](int d) { return d == RB_F32 || d == RB_BF16 || d == RB_F16; };
+  if (sa == nullptr || sb == nullptr || !fdt(sa_dtype) || !fdt(sb_dtype) || (bias != nullptr && !fdt(bias_dtype)))
+    return fail(RB_ERR_VALUE, "scales (and bias) must be given as f32/bf16/f16");
+  if (!aligned(sb, 16) || (bias != nullptr && !aligned(bias, 16)))
+    return fail(RB_ERR_VALUE, "per-channel scales and bias must be 16-byte aligned");
+  if (ln_gamma == nullptr || ln_beta == nullptr || !fdt(ln_dtype))
+    return fail(RB_ERR_VALUE, "LayerNorm gamma/beta must be given as f32/bf16/f16");
+  if (!aligned(ln_gamma, 16) || !aligned(ln_beta, 16)) return fail(RB_ERR_VALUE, "gamma/beta must be 16-byte aligned");
+  if (!aligned(out, 16) || (ldo * dtype_size(out_dtype)) % 16 != 0)
+    return fail(RB_ERR_VALUE, "out rows must be 16-byte aligned");
+  if (M > 0x7fffffffLL || K > 0x7fffffffLL) return fail(RB_ERR_UNSUPPORTED, "dimension above 2^31-1");
+  if (!device_is_sm100()) return fail(RB_ERR_DEVICE, "rb_w8a8_gemm_ln needs an sm_100 (B200) device");
+  if (!(K > 0 && K % 16 == 0 && lda % 16 == 0 && ldb % 16 == 0 && aligned(A, 16) && aligned(B, 16)))
+    return fail(RB_ERR_UNSUPPORTED, "rb_w8a8_gemm_ln needs K %% 16 == 0 and 16-byte aligned operand rows");
+  EpiParams ep{};
+  ep.sa = sa;
+  ep.sb = sb;
+  ep.bias = bias;
+  ep.out = out;
+  ep.ldo = ldo;
+  ep.M = M;
+  ep.N = N;
+  ep.K = K;
+  ep.sa_dtype = sa_dtype;
+  ep.sa_per_row = sa_per_row;
+  ep.sb_dtype = sb_dtype;
+  ep.bias_dtype = bias_dtype;
+  ep.out_dtype = out_dtype;
+  ep.ksplits = 1;
+  pair::LnParams lp{};
+  lp.gamma = ln_gamma;
+  lp.beta = ln_beta;
+  lp.ln_dtype = ln_dtype;
+  lp.eps = eps;
+  lp.out = ln_out;
+  lp.ldo = ldl;
+  CUtensorMap tpA, tpB;
+  int rc = make_tmap(&tpA, A, K, M, lda, pair::BK, 128);
+  if (rc) return rc;
+  rc = make_tmap(&tpB, B, K, N, ldb, pair::BK, 128);
+  if (rc) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t pe = cudaSuccess;
+  std::call_once(g_ln_attr_once[dev & 63], [&] {
+    pe = cudaFuncSetAttribute(pair::w8a8_gemm_ln_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              pair::LN_SMEM_BYTES);
+  });
+  if (pe != cudaSuccess) return check_cuda(pe, "cudaFuncSetAttribute(w8a8_gemm_ln_pair_kernel)");
+  const int64_t tiles = (M + pair::BM - 1) / pair::BM;
+  const int pairs = (int)std::min<int64_t>(tiles, sm_count() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(pair::NUM_THREADS);
+  cfg.dynamicSmemBytes = pair::LN_SMEM_BYTES;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, pair::w8a8_gemm_ln_pair_kernel, tpA, tpB, ep, lp),
+                    "w8a8_gemm_ln_pair_kernel launch");
 }
 
 // ----------------------------------------------------------------------------

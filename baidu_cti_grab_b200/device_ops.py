@@ -387,6 +387,33 @@ def w8a8_gemm(a: torch.Tensor, b_nk: torch.Tensor, scale_a: Optional[torch.Tenso
     return out
 
 
+def w8a8_gemm_ln(a: torch.Tensor, b_nk: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,
+                 out: torch.Tensor, ln_gamma: torch.Tensor, ln_beta: torch.Tensor, eps: float, ln_out: torch.Tensor,
+                 *, bias: Optional[torch.Tensor] = None, sa_per_row: bool = True):
+    """out = ((f32(A @ B^T) * sa) * sb) + bias and ln_out = LayerNorm(out) over its 512
+    columns (rb_w8a8_gemm_ln).  Returns (out, ln_out)."""
+    dev = require_cuda("w8a8_gemm_ln", a, b_nk, out, ln_out, scale_a, scale_b, bias, ln_gamma, ln_beta)
+    if a.dim() != 2 or b_nk.dim() != 2 or a.stride(1) != 1 or b_nk.stride(1) != 1 or out.stride(1) != 1 \
+            or ln_out.stride(1) != 1:
+        raise ValueError("w8a8_gemm_ln expects row-major 2-D operands")
+    M, K = a.shape
+    N = b_nk.shape[0]
+    if b_nk.shape[1] != K:
+        raise ValueError(f"shape mismatch: A K={K}, B K={b_nk.shape[1]}")
+    if tuple(out.shape) != (M, N) or tuple(ln_out.shape) != (M, N) or ln_out.dtype != out.dtype:
+        raise ValueError(f"out and ln_out must be [{M}, {N}] of one dtype")
+    scale_a, scale_b = scale_a.contiguous(), scale_b.contiguous()
+    bias = None if bias is None else bias.contiguous()
+    ln_gamma, ln_beta = ln_gamma.contiguous(), ln_beta.contiguous()
+    with torch.cuda.device(dev):
+        L.call("rb_w8a8_gemm_ln", a.data_ptr(), a.stride(0), b_nk.data_ptr(), b_nk.stride(0), M, N, K,
+               scale_a.data_ptr(), rb_dtype(scale_a), 1 if sa_per_row else 0, scale_b.data_ptr(), rb_dtype(scale_b),
+               _ptr(bias), rb_dtype(bias) if bias is not None else 0, out.data_ptr(), out.stride(0), rb_dtype(out),
+               ln_gamma.data_ptr(), ln_beta.data_ptr(), rb_dtype(ln_gamma), float(eps), ln_out.data_ptr(),
+               ln_out.stride(0), _stream(dev))
+    return out, ln_out
+
+
 def fp_gemm(a: torch.Tensor, b_nk: torch.Tensor, out: torch.Tensor, *,
             bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     """out = A @ B^T + bias on the tensor cores: A [M, K], B [N, K] both bf16

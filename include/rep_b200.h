@@ -233,6 +233,23 @@ int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, 
                     int32_t* workspace, int64_t workspace_elems, void* stream);
 
 /*
+ * rb_w8a8_gemm with the transformer's first LayerNorm fused into the epilogue
+ * (models.py:216-217: layer 0 begins residual = x; x = norm1[0](x), x being
+ * the RepEncoder output this GEMM produces).  out is rb_w8a8_gemm's result
+ * (the residual), ln_out = LayerNorm(out) over the 512 columns with
+ * ln_gamma/ln_beta (ln_dtype RB_F32/RB_BF16/RB_F16) and eps, in the reduction
+ * order of ATen's CUDA LayerNorm, so it equals nn.LayerNorm on out bit for
+ * bit.  N must be 512; out and ln_out share out_dtype (RB_BF16/RB_F16/RB_F32);
+ * sb and bias 16-byte aligned.  Replaces quantization/w8a8_triton_kernels.py's
+ * scaled GEMM (:470-564) followed by the first norm1 of models.py:217.
+ */
+int rb_w8a8_gemm_ln(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M, int64_t N,
+                    int64_t K, const void* sa, int sa_dtype, int sa_per_row, const void* sb, int sb_dtype,
+                    const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
+                    const void* ln_gamma, const void* ln_beta, int ln_dtype, float eps, void* ln_out,
+                    int64_t ldl, void* stream);
+
+/*
  * Unquantised Linear on the tensor cores: out[m,n] = sum_k A[m,k] * B[n,k] + bias[n].
  * Replaces the GEMM of kernels/rep_encoder_fusion.py:33-112 (_layernorm_linear_kernel,
  * a tl.dot of bf16 operands -- or fp32 operands, which Triton multiplies as tf32 --
