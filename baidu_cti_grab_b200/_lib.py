@@ -54,6 +54,9 @@ SIGNATURES = {
     "rb_w8a8_gemm_ln": [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _i32, _vp, _i32, _vp,
                         _i64, _i32, _vp, _vp, _i32, _f32, _vp, _i64, _vp],
     "rb_fp_gemm": [_vp, _i32, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _vp, _i64, _i32, _vp],
+    "rb_smoe_workspace_size": [_i64, _i32, _i32, _i32, _i32, _i32],
+    "rb_smoe_experts": [_vp, _i32, _i64, _i64, _i32, _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp,
+                        _i64, _vp, _i64, _vp],
     "rb_rep_gather_pool_scatter": [_vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _i64, _vp, _vp, _i32, _i64,
                                    _i64, _vp],
     "rb_ipc_export": [_vp, _vp, _vp],
@@ -65,7 +68,7 @@ SIGNATURES = {
     "rb_version": [],
 }
 
-RETURNS_I64 = {"rb_w8a8_gemm_workspace_size"}
+RETURNS_I64 = {"rb_w8a8_gemm_workspace_size", "rb_smoe_workspace_size"}
 
 _lock = threading.Lock()
 _lib: Optional[ctypes.CDLL] = None

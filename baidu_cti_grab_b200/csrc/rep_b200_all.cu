@@ -4,4 +4,5 @@
 #include "rep_fused.cu"
 #include "quant.cu"
 #include "gemm_tc.cu"
+#include "moe.cu"
 #include "peer.cu"

@@ -438,6 +438,61 @@ def fp_gemm(a: torch.Tensor, b_nk: torch.Tensor, out: torch.Tensor, *,
     return out
 
 
+_SMOE_WS: Dict[Tuple[int, int], torch.Tensor] = {}
+
+
+def smoe_experts(x: torch.Tensor, topk_idx: torch.Tensor, topk_score: torch.Tensor, w1: torch.Tensor,
+                 b1: Optional[torch.Tensor], w2: torch.Tensor, b2: Optional[torch.Tensor],
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The SMoE expert layer after the gate (rb_smoe_experts).
+
+    x [T, D] bf16/f16; topk_idx [T, k] int64/int32; topk_score [T, k] in x.dtype;
+    w1 [E, F, D], b1 [E, F], w2 [E, D, F], b2 [E, D] in x.dtype.
+    Returns out [T, D] = sum over each token's k experts of
+    score * (relu(x W1^T + b1) W2^T + b2)."""
+    dev = require_cuda("smoe_experts", x, topk_idx, topk_score, w1, b1, w2, b2, out)
+    if x.dim() != 2 or topk_idx.dim() != 2 or topk_score.shape != topk_idx.shape:
+        raise ValueError("smoe_experts expects x [T, D] and topk_idx/topk_score [T, k]")
+    T, D = x.shape
+    k = topk_idx.shape[1]
+    if topk_idx.shape[0] != T:
+        raise ValueError("topk_idx must have one row per token")
+    if w1.dim() != 3 or w2.dim() != 3 or w1.shape[2] != D or w2.shape[1] != D or w2.shape[0] != w1.shape[0] \
+            or w2.shape[2] != w1.shape[1]:
+        raise ValueError("w1 must be [E, F, D] and w2 [E, D, F]")
+    E, F = w1.shape[0], w1.shape[1]
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("smoe_experts takes bf16 or f16 activations")
+    if topk_idx.dtype not in (torch.int64, torch.int32):
+        raise ValueError("topk_idx must be int64 or int32")
+    if any(t is not None and t.dtype != x.dtype for t in (topk_score, w1, b1, w2, b2)):
+        raise ValueError("scores, weights and biases must share x's dtype")
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    topk_idx, topk_score = topk_idx.contiguous(), topk_score.contiguous()
+    w1, w2 = w1.contiguous(), w2.contiguous()
+    b1 = None if b1 is None else b1.contiguous()
+    b2 = None if b2 is None else b2.contiguous()
+    if out is None:
+        out = torch.empty((T, D), dtype=x.dtype, device=dev)
+    elif tuple(out.shape) != (T, D) or out.dtype != x.dtype or out.stride(1) != 1:
+        raise ValueError(f"out must be a row-major [{T}, {D}] {x.dtype} tensor")
+    lib = L.load()
+    idt = L.RB_I64 if topk_idx.dtype == torch.int64 else L.RB_I32
+    need = int(lib.rb_smoe_workspace_size(T, k, E, D, F, rb_dtype(x)))
+    if need < 0:
+        raise ValueError("rb_smoe_workspace_size rejected the shape")
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    ws = _SMOE_WS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = _SMOE_WS[key] = torch.empty((max(need, 256),), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        L.call("rb_smoe_experts", x.data_ptr(), rb_dtype(x), x.stride(0), T, D, topk_idx.data_ptr(), idt,
+               topk_score.data_ptr(), k, E, w1.data_ptr(), _ptr(b1), w2.data_ptr(), _ptr(b2), F, ws.data_ptr(),
+               ws.numel(), out.data_ptr(), out.stride(0), _stream(dev))
+    return out
+
+
 def device_error(reset: bool = False) -> int:
     return L.device_error(reset)
 

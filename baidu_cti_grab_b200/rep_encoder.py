@@ -95,12 +95,23 @@ def _quantized_weight(rep: nn.Module):
     return q_nk, w_scale, lin.bias, None
 
 
+def _fusable_norm(norm, d_model: int, dtype: torch.dtype) -> bool:
+    return (norm is not None and d_model == 512 and dtype in (torch.bfloat16, torch.float16, torch.float32)
+            and getattr(norm, "weight", None) is not None and getattr(norm, "bias", None) is not None
+            and tuple(getattr(norm, "normalized_shape", ())) == (512,))
+
+
 def rep_encoder_forward(rep: nn.Module, batch, act_mode: Optional[str] = None,
-                        return_intermediates: bool = False, out: Optional[torch.Tensor] = None):
+                        return_intermediates: bool = False, out: Optional[torch.Tensor] = None,
+                        norm: Optional[nn.Module] = None):
     """Fused B200 forward of a RepEncoder-shaped module on a reference batch dict.
 
     Returns rep_emb [N, d_model] in the table dtype (written into ``out`` when
-    given), and with return_intermediates a dict with q, scale, pooled and ln."""
+    given), and with return_intermediates a dict with q, scale, pooled and ln.
+    With ``norm`` (the transformer's first nn.LayerNorm(512), models.py:216-217)
+    the GEMM also applies it in its epilogue (rb_w8a8_gemm_ln) and the call
+    returns (rep_emb, norm(rep_emb)) -- bit-identical to running the module on
+    rep_emb."""
     table = rep.emb.weight
     device = table.device
     if device.type != "cuda":
@@ -125,11 +136,18 @@ def rep_encoder_forward(rep: nn.Module, batch, act_mode: Optional[str] = None,
     elif tuple(out.shape) != (n, w_nk.shape[0]) or out.dtype != table.dtype:
         raise ValueError(f"out must be [{n}, {w_nk.shape[0]}] {table.dtype}")
     sa = scale if act_mode == "dynamic" else static_scale
-    device_ops.w8a8_gemm(q, w_nk, sa, w_scale, out, bias=None if bias is None else bias.detach(),
-                         sa_per_row=(act_mode == "dynamic"))
+    bias_d = None if bias is None else bias.detach()
+    if norm is not None and _fusable_norm(norm, w_nk.shape[0], out.dtype):
+        normed = torch.empty_like(out)
+        device_ops.w8a8_gemm_ln(q, w_nk, sa, w_scale, out, norm.weight.detach(), norm.bias.detach(), norm.eps,
+                                normed, bias=bias_d, sa_per_row=(act_mode == "dynamic"))
+    else:
+        device_ops.w8a8_gemm(q, w_nk, sa, w_scale, out, bias=bias_d, sa_per_row=(act_mode == "dynamic"))
+        normed = None if norm is None else norm(out)
+    res = out if norm is None else (out, normed)
     if return_intermediates:
-        return out, {"q": q, "scale": scale, "pooled": pooled, "ln": ln_out}
-    return out
+        return res, {"q": q, "scale": scale, "pooled": pooled, "ln": ln_out}
+    return res
 
 
 class RepEncoder(nn.Module):
@@ -172,20 +190,27 @@ class RepEncoder(nn.Module):
 
 
 def install(models_module) -> None:
-    """Add fuse_mode "b200" to a reference ``models`` module's RepEncoder.forward.
+    """Add fuse_mode "b200" to a reference ``models`` module.
 
     After ``install(models)``, ``models.load_model(..., rep_fuse_mode="b200")``
-    and ``infer.py --rep-fuse-mode b200`` run this package's kernels; every
+    and ``infer.py --rep-fuse-mode b200`` run this package's kernels:
+    RepEncoder.forward runs K1 + K2; CTRModel.forward, when its RepEncoder is
+    in b200 mode, takes the encoder's first LayerNorm (norm1[0],
+    models.py:216-217) from K2's fused epilogue, builds the attention
+    extension without a mid-forward host sync and runs every SMoE layer
+    through the grouped expert kernels (ctr_boundary.install_ctr).  Every
     other fuse mode keeps the reference's own code path."""
     cls = models_module.RepEncoder
-    if getattr(cls, "_b200_installed", False):
-        return
-    original = cls.forward
+    if not getattr(cls, "_b200_installed", False):
+        original = cls.forward
 
-    def forward(self, batch):
-        if getattr(self, "fuse_mode", None) == FUSE_MODE:
-            return rep_encoder_forward(self, batch)
-        return original(self, batch)
+        def forward(self, batch):
+            if getattr(self, "fuse_mode", None) == FUSE_MODE:
+                return rep_encoder_forward(self, batch)
+            return original(self, batch)
 
-    cls.forward = forward
-    cls._b200_installed = True
+        cls.forward = forward
+        cls._b200_installed = True
+    from .ctr_boundary import install_ctr
+
+    install_ctr(models_module)

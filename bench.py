@@ -83,6 +83,7 @@ def parse_args(argv=None):
                     help="--impl reference: items of the batch each CPU step processes")
     ap.add_argument("--no-reference-gpu", action="store_true")
     ap.add_argument("--no-uniform-k1", action="store_true")
+    ap.add_argument("--no-smoe", action="store_true", help="skip the SMoE expert-layer measurement")
     return ap.parse_args(argv)
 
 
@@ -485,6 +486,68 @@ def reference_gpu_forward(table, vals, offs, gamma, beta, eps, w_nk, w_scale, bi
     return w8a8, bf16_linear
 
 
+def reference_smoe_torch(x, idx, score, w1_kn, b1, w2_kn, b2):
+    """The reference's SMoE expert step (models.py:137-172) in torch: stable
+    argsort by expert, a zero-padded [E, max_count, D] block sized by a host
+    read of the largest count, two bmm's with [E, K, N] stacked weights,
+    index_add_ of the score-weighted rows."""
+    import torch
+
+    T, D = x.shape
+    k = idx.shape[1]
+    E = w1_kn.shape[0]
+    route_expert = idx.reshape(-1)
+    route_token = torch.arange(T, device=x.device).repeat_interleave(k)
+    order = torch.argsort(route_expert, stable=True)
+    se, sw, st = route_expert[order], score.reshape(-1)[order], route_token[order]
+    counts = torch.bincount(se, minlength=E)
+    starts = torch.cumsum(counts, 0) - counts
+    pos = torch.arange(se.numel(), device=x.device) - torch.repeat_interleave(starts, counts)
+    packed = x.new_zeros((E, int(counts.max().item()), D))
+    packed[se, pos] = x[st]
+    hidden = torch.relu(torch.bmm(packed, w1_kn) + b1.unsqueeze(1))
+    pout = torch.bmm(hidden, w2_kn) + b2.unsqueeze(1)
+    out = torch.zeros_like(x)
+    out.index_add_(0, st, pout[se, pos] * sw.unsqueeze(-1))
+    return out
+
+
+def smoe_measure(dev, tokens: int, bf16_peak: float) -> dict:
+    """Device time of rb_smoe_experts and of the reference's torch formulation
+    at `tokens` tokens (d_model 512, dim_ff 1024, 8 experts, top-2 -- the
+    encoder of load_model), bf16, random weights and gate scores."""
+    import torch
+    from baidu_cti_grab_b200 import device_ops
+
+    D, F, E, k = 512, 1024, 8, 2
+    gen = torch.Generator(device=dev).manual_seed(77)
+    bf = torch.bfloat16
+    x = torch.randn(tokens, D, device=dev, generator=gen).to(bf)
+    probs = torch.softmax(torch.randn(tokens, E, device=dev, generator=gen).to(bf), dim=-1)
+    score, idx = torch.topk(probs, k, dim=-1)
+    w1 = (torch.randn(E, F, D, device=dev, generator=gen) / D ** 0.5).to(bf)
+    w2 = (torch.randn(E, D, F, device=dev, generator=gen) / F ** 0.5).to(bf)
+    b1 = (0.1 * torch.randn(E, F, device=dev, generator=gen)).to(bf)
+    b2 = (0.1 * torch.randn(E, D, device=dev, generator=gen)).to(bf)
+    out = torch.empty_like(x)
+    ms = time_cuda(lambda: device_ops.smoe_experts(x, idx, score, w1, b1, w2, b2, out=out), reps=10)
+    w1_kn, w2_kn = w1.transpose(1, 2).contiguous(), w2.transpose(1, 2).contiguous()
+    ref_ms = time_cuda(lambda: reference_smoe_torch(x, idx, score, w1_kn, b1, w2_kn, b2), reps=5, warmup=2)
+    ref = reference_smoe_torch(x, idx, score, w1_kn, b1, w2_kn, b2)
+    rel = float((out.float() - ref.float()).norm() / ref.float().norm())
+    flops = 4.0 * tokens * k * D * F
+    tflops = flops / (ms * 1e-3) / 1e12
+    return {"kernel": "rb_smoe_experts (route + pack, two grouped tcgen05 kind::f16 GEMMs, combine)",
+            "tokens": tokens, "d_model": D, "dim_ff": F, "experts": E, "top_k": k, "avg_ms": round(ms, 4),
+            "achieved": round(tflops, 1), "unit": "TFLOP/s", "peak": bf16_peak,
+            "frac": round(tflops * 1e12 / (bf16_peak * 1e12), 4) if bf16_peak else None,
+            "peak_source": "measured bf16 (burst)",
+            "reference_torch_ms": round(ref_ms, 4), "speedup_vs_reference_torch": round(ref_ms / ms, 2),
+            "rel_l2_vs_reference_torch": round(rel, 6),
+            "what": "the expert layer after the gate; reference_torch = models.py:137-172 on ATen/cuBLAS "
+                    "(argsort, padded [E, max_count, D] block sized by a host read, two bmm, index_add_)"}
+
+
 def b200_arm(args):
     import torch
     import torch.distributed as dist
@@ -647,6 +710,14 @@ def b200_arm(args):
         del w8a8_fn, bf16_fn
         torch.cuda.empty_cache()
 
+    # ---- the SMoE expert layer of the encoder (models.py:131-178) at this
+    # batch's token count: the grouped expert kernels against the reference's
+    # torch formulation (padded bmm's on cuBLAS) on the same inputs (rank 0)
+    smoe = None
+    if world == 1 and not args.no_smoe:
+        smoe = smoe_measure(dev, stats[0][0], measured_peaks()[1])
+        torch.cuda.empty_cache()
+
     # ---- e2e through the public API from pinned host memory: packed host
     # batches, H2D / forward / D2H of successive batches overlapped on streams
     e2e = None
@@ -776,6 +847,8 @@ def b200_arm(args):
             line["kernels"]["k1_uniform"] = k1_uniform
         if reference_gpu is not None:
             line["reference_gpu"] = reference_gpu
+        if smoe is not None:
+            line["kernels"]["smoe"] = smoe
 
     # ---- CPU baseline (rank 0, N=1 only)
     if world > 1:

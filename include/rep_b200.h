@@ -282,6 +282,32 @@ int rb_w8a8_gemm_noalloc(const int8_t* A, int64_t lda, const int8_t* B, int64_t 
                          int64_t K, const void* sa, int sa_dtype, int sa_per_row, const void* sb, int sb_dtype,
                          const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype, void* stream);
 
+/*
+ * The SMoE expert layer after the gate (models.py:131-178: sort the routed
+ * entries by expert, pack, two bmm's with the stacked expert weights, relu,
+ * score weighting, index_add_), without a host read of the per-expert counts
+ * (models.py:160) and without padding rows.
+ *   x          [T, ldx] RB_BF16 or RB_F16 (the model dtype), d_model = D
+ *   topk_idx   [T, k] contiguous, RB_I64 (torch.topk's output) or RB_I32,
+ *              expert ids in [0, E); an id outside it adds nothing and sets
+ *              the device error word (rb_device_error)
+ *   topk_score [T, k] contiguous gate scores in the model dtype
+ *   w1 [E, F, D], b1 [E, F] or NULL (each expert's fc1 nn.Linear weight and
+ *   bias, stacked), w2 [E, D, F], b2 [E, D] or NULL (fc2), all in the model
+ *   dtype; D and F multiples of 64, E <= 64
+ *   workspace  rb_smoe_workspace_size(T, k, E, D, F, x_dtype) bytes, 256-byte aligned
+ *   out        [T, ldo], 32-byte aligned rows; every row written
+ * Each expert output is rounded to the model dtype where the reference's
+ * torch ops round (bmm, + bias, * score, the index_add_ sum); the fp32
+ * accumulation order inside the dot products is this library's own.
+ * rb_smoe_workspace_size returns -1 for an invalid shape or dtype.
+ */
+int64_t rb_smoe_workspace_size(int64_t T, int k, int E, int D, int F, int x_dtype);
+int rb_smoe_experts(const void* x, int x_dtype, int64_t ldx, int64_t T, int D, const void* topk_idx,
+                    int idx_dtype, const void* topk_score, int k, int E, const void* w1, const void* b1,
+                    const void* w2, const void* b2, int F, void* workspace, int64_t workspace_bytes,
+                    void* out, int64_t ldo, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
