@@ -36,12 +36,12 @@ def quantize_rows_int8_triton(x):
 
 
 def quantize_weight_per_channel_int8(weight):
-    """Symmetric per-output-channel INT8 quantization for Linear weights."""
+    """A Linear weight [N, K] quantised row by row (one scale per output channel)."""
     return quantize_rows_int8_triton(weight)
 
 
 def quantize_activation_per_token_int8(x):
-    """Symmetric per-token INT8 activation quantization."""
+    """Activations [M, K] quantised row by row (one scale per token)."""
     return quantize_rows_int8_triton(x)
 
 
@@ -71,20 +71,17 @@ def _linear_v1(name, x, weight_int8, weight_scale, bias, out_dtype):
 
 def w8a8_linear_triton_dynamic_unfused(x, weight_int8, weight_scale, bias=None, out_dtype=torch.bfloat16,
                                        block_m=32, block_n=64, block_k=64, group_m=8, autotune=False):
-    """Dynamic W8A8 Linear: per-row activation quantisation, then the int8 GEMM.
-
-    Args:
-        x: [M, K] floating point activation.
-        weight_int8: [N, K] int8 weight.
-        weight_scale: [N] fp32 per-output-channel scale.
-        bias: optional [N] bias.
-    """
+    """x [M, K] (float) -> [M, N] out_dtype: rows quantised once (rb_quant_rows_v1),
+    then the tcgen05 int8 GEMM with acc * x_scale[m] * weight_scale[n] + bias[n];
+    weight_int8 is [N, K], weight_scale [N] fp32, bias [N] or None."""
     return _linear_v1("w8a8_linear_triton_dynamic_unfused", x, weight_int8, weight_scale, bias, out_dtype)
 
 
 def w8a8_linear_triton_dynamic_fused(x, weight_int8, weight_scale, bias=None, out_dtype=torch.bfloat16,
                                      block_m=32, block_n=64, block_k=64, group_m=8):
-    """Dynamic W8A8 Linear with on-the-fly activation quantisation."""
+    """The reference's single-kernel variant: same arguments and the same output
+    bits as the two-kernel one, which this build runs for both (each row is
+    quantised once instead of once per output tile)."""
     return _linear_v1("w8a8_linear_triton_dynamic_fused", x, weight_int8, weight_scale, bias, out_dtype)
 
 
