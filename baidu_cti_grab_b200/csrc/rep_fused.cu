@@ -239,13 +239,22 @@ struct Affine<float> {
   __device__ __forceinline__ F2 beta(int i, bool) const { return f2(b[2 * i], b[2 * i + 1]); }
 };
 
-// A bf16 table row of -0.0.  x + (-0.0) == x for every fp32 x (+0 and -0
-// included), so a padding id, or a position past the end of a bag, reads this
-// row and is added like any other instead of being branched around.
+// Table rows of -0.0 (bf16 and fp32).  x + (-0.0) == x for every fp32 x (+0
+// and -0 included), so a padding id, or a position past the end of a bag,
+// reads this row and is added like any other instead of being branched around.
 #define RB_NZ4 0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u
 #define RB_NZ16 RB_NZ4, RB_NZ4, RB_NZ4, RB_NZ4
 #define RB_NZ64 RB_NZ16, RB_NZ16, RB_NZ16, RB_NZ16
 static __device__ __align__(16) const uint32_t g_negzero_row_bf16[kDim / 2] = {RB_NZ64, RB_NZ64, RB_NZ64, RB_NZ64};
+#define RB_NZF4 0x80000000u, 0x80000000u, 0x80000000u, 0x80000000u
+#define RB_NZF16 RB_NZF4, RB_NZF4, RB_NZF4, RB_NZF4
+#define RB_NZF64 RB_NZF16, RB_NZF16, RB_NZF16, RB_NZF16
+#define RB_NZF256 RB_NZF64, RB_NZF64, RB_NZF64, RB_NZF64
+static __device__ __align__(16) const uint32_t g_negzero_row_f32[kDim] = {RB_NZF256, RB_NZF256};
+#undef RB_NZF256
+#undef RB_NZF64
+#undef RB_NZF16
+#undef RB_NZF4
 #undef RB_NZ64
 #undef RB_NZ16
 #undef RB_NZ4
@@ -337,6 +346,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
   extern __shared__ __align__(16) uint8_t s_raw[];
   __shared__ float s_stat[4];  // Welford (mean, m2) of chain groups {0,2} and {1,3}
   __shared__ float s_wmax[kMaxWarps];
+  __shared__ const T* s_rowptr[kMaxWarps * 32];  // per pooling warp: row addresses of its id window
   uint32_t* s_words = reinterpret_cast<uint32_t*>(s_raw);  // bf16 row: 256 words per slot
   float* s_f32 = reinterpret_cast<float*>(s_raw);          // fp32 row: 512 floats per slot
 
@@ -430,39 +440,54 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
         bound = (IdxT)(b < 0 ? 0 : (b > nz ? nz : b));
       }
     }
+    // each bag's positions padded to a multiple of kRows: slot j of the warp
+    // owns positions pre[j] .. pre[j+1]-1 of the warp's position list, its
+    // first len[j] positions the bag's ids, the rest the -0.0 row
     IdxT start[kSlotsPerWarp];
+    int len[kSlotsPerWarp];
     int pre[kSlotsPerWarp + 1];
     int total = 0;
 #pragma unroll
     for (int j = 0; j < kSlotsPerWarp; ++j) {
       start[j] = shfl_idx(bound, j);
       const IdxT e = shfl_idx(bound, kSlotsPerWarp + j);
+      len[j] = (j < nsl && e > start[j]) ? (int)(e - start[j]) : 0;
       pre[j] = total;
-      total += (j < nsl && e > start[j]) ? (int)(e - start[j]) : 0;
+      total += (len[j] + kRows - 1) / kRows * kRows;
     }
     pre[kSlotsPerWarp] = total;
 
     const T* table = reinterpret_cast<const T*>(p.table);
+    const T* const pad_row = kBf16 ? reinterpret_cast<const T*>(g_negzero_row_bf16)
+                                   : reinterpret_cast<const T*>(g_negzero_row_f32);
     const int vmax = (int)(p.num_rows - 1);
-    // ids of flattened positions w0 .. w0+31, one per lane; each row is
-    // requested into L2 as soon as its id is known
+    // row addresses of positions w0 .. w0+31 into the warp's pointer list (one
+    // per lane); each table row is requested into L2 as soon as its id is known
+    const T** const wptr = s_rowptr + warp * 32;
     auto load_window = [&](int w0) {
       const int t = w0 + lane;
-      int id = 0;
+      const T* row = pad_row;
       if (t < total) {
         int j = 0;
 #pragma unroll
         for (int i = 1; i < kSlotsPerWarp; ++i) j += t >= pre[i];
-        const int64_t v =
-            static_cast<const IdxT*>(p.slots.values[slot_of(j)])[(int64_t)sel<kSlotsPerWarp>(start, j) +
-                                                                 (t - sel<kSlotsPerWarp>(pre, j))];
-        id = (int)(v < 0 ? 0 : (v > vmax ? vmax : v));
-        if (id != 0) prefetch_l2_bulk(table + (int64_t)id * kDim, kDim * (int)sizeof(T));
+        const int k = t - sel<kSlotsPerWarp>(pre, j);
+        if (k < sel<kSlotsPerWarp>(len, j)) {
+          const int64_t v =
+              static_cast<const IdxT*>(p.slots.values[slot_of(j)])[(int64_t)sel<kSlotsPerWarp>(start, j) + k];
+          const int id = (int)(v < 0 ? 0 : (v > vmax ? vmax : v));
+          if (id != 0) {
+            row = table + (int64_t)id * kDim;
+            prefetch_l2_bulk(row, kDim * (int)sizeof(T));
+          }
+        }
       }
-      return id;
+      __syncwarp();  // every lane is done reading the previous window
+      wptr[lane] = row;
+      __syncwarp();
     };
     int w0 = 0;
-    int my_id = load_window(0);
+    load_window(0);
 
 #pragma unroll
     for (int j = 0; j < kSlotsPerWarp; ++j) {
@@ -472,24 +497,20 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
 #pragma unroll
       for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
       for (int t = pre[j]; t < tend; t += kRows) {
-        if (t + kRows > w0 + 32) {  // warp-uniform: slide the id window
+        if (t + kRows > w0 + 32) {  // warp-uniform: slide the window
           w0 = t;
-          my_id = load_window(w0);
+          load_window(w0);
         }
-        int ids[kRows];
+        // the kRows row addresses (a broadcast read: every lane reads the same entries)
+        const T* rows[kRows];
 #pragma unroll
-        for (int u = 0; u < kRows; ++u) {
-          ids[u] = __shfl_sync(0xffffffffu, my_id, (t + u - w0) & 31);
-          if (t + u >= tend) ids[u] = 0;
-        }
+        for (int u = 0; u < kRows; ++u) rows[u] = wptr[t - w0 + u];
         if constexpr (kBf16) {
           uint32_t buf[kRows][8];
-          // padding_idx 0 (and positions past the bag) add the -0.0 row: no branch
+          // a padding id (0, or a negative id clamped to 0) and the positions past
+          // the bag add the -0.0 row: no branch
 #pragma unroll
-          for (int u = 0; u < kRows; ++u)
-            ldg_words(ids[u] != 0 ? static_cast<const void*>(table + (int64_t)ids[u] * kDim)
-                                  : static_cast<const void*>(g_negzero_row_bf16),
-                      lane, buf[u]);
+          for (int u = 0; u < kRows; ++u) ldg_words(rows[u], lane, buf[u]);
 #pragma unroll
           for (int u = 0; u < kRows; ++u) {
 #pragma unroll
@@ -501,17 +522,14 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
         } else {
           F2 buf[kRows][8];
 #pragma unroll
-          for (int u = 0; u < kRows; ++u)
-            if (ids[u] != 0) ldg_pairs(reinterpret_cast<const float*>(table) + (int64_t)ids[u] * kDim, lane, buf[u]);
+          for (int u = 0; u < kRows; ++u) ldg_pairs(reinterpret_cast<const float*>(rows[u]), lane, buf[u]);
 #pragma unroll
           for (int u = 0; u < kRows; ++u) {
-            if (ids[u] != 0) {
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float2 v = un(buf[u][i]);
-                acc[2 * i] = __fadd_rn(acc[2 * i], v.x);
-                acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], v.y);
-              }
+            for (int i = 0; i < 8; ++i) {
+              const float2 v = un(buf[u][i]);
+              acc[2 * i] = __fadd_rn(acc[2 * i], v.x);
+              acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], v.y);
             }
           }
         }
