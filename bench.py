@@ -718,6 +718,32 @@ def b200_arm(args):
         smoe = smoe_measure(dev, stats[0][0], measured_peaks()[1])
         torch.cuda.empty_cache()
 
+    # ---- K2 with the encoder's first LayerNorm(512) in its epilogue (the
+    # RepEncoder -> Transformer boundary, models.py:216-217) against K2 followed
+    # by ATen's layer_norm, on the first batch's int8 activations (rank 0)
+    k2_ln = None
+    if world == 1 and not args.no_smoe:
+        import torch.nn.functional as F
+
+        n0 = stats[0][0]
+        q0, s0, _ = step(0)
+        g512 = (1 + 0.1 * torch.randn(D_OUT, device=dev, generator=gen)).to(bf)
+        b512 = (0.1 * torch.randn(D_OUT, device=dev, generator=gen)).to(bf)
+        ln_buf = torch.empty_like(out_buf[:n0])
+        fused_ms = time_cuda(lambda: device_ops.w8a8_gemm_ln(q0, w_nk, s0, w_scale, out_buf[:n0], g512, b512, 1e-5,
+                                                              ln_buf, bias=bias), reps=10)
+        split_ms = time_cuda(lambda: (gemm(q0, s0, n0), F.layer_norm(out_buf[:n0], (D_OUT,), g512, b512, 1e-5)),
+                             reps=10)
+        ref_ln = F.layer_norm(out_buf[:n0], (D_OUT,), g512, b512, 1e-5)
+        device_ops.w8a8_gemm_ln(q0, w_nk, s0, w_scale, out_buf[:n0], g512, b512, 1e-5, ln_buf, bias=bias)
+        k2_ln = {"kernel": "w8a8_gemm_ln_kernel (K2 with LayerNorm(512) of each output row in the epilogue)",
+                 "items": n0, "avg_ms": round(fused_ms, 4), "k2_then_aten_layer_norm_ms": round(split_ms, 4),
+                 "achieved": round(k2_ops(n0) / (fused_ms * 1e-3) / 1e12, 1), "unit": "TOP/s",
+                 "ln_equal_to_aten": bool(torch.equal(ln_buf, ref_ln)),
+                 "what": "rb_w8a8_gemm_ln: the GEMM output and its LayerNorm(512) (models.py:216-217) from one "
+                         "kernel, against rb_w8a8_gemm + F.layer_norm on the same operands"}
+        del ln_buf
+
     # ---- e2e through the public API from pinned host memory: packed host
     # batches, H2D / forward / D2H of successive batches overlapped on streams
     e2e = None
@@ -849,6 +875,8 @@ def b200_arm(args):
             line["reference_gpu"] = reference_gpu
         if smoe is not None:
             line["kernels"]["smoe"] = smoe
+        if k2_ln is not None:
+            line["kernels"]["k2_ln"] = k2_ln
 
     # ---- CPU baseline (rank 0, N=1 only)
     if world > 1:
