@@ -83,7 +83,7 @@ def main() -> int:
         sub = sharding.slice_items(batch, i0, i1)
         sv = [torch.from_numpy(sub[s][0]).to(dev) for s in range(1, 29)]
         so = [torch.from_numpy(sub[s][1]).to(dev) for s in range(1, 29)]
-        q, scale = device_ops.rep_gather_ln_quant(full, sv, so, gamma, beta, 1e-5)
+        q, scale, _, _ = device_ops.rep_gather_ln_quant(full, sv, so, gamma, beta, 1e-5)
         out_single = device_ops.w8a8_gemm(q, w_nk, scale, w_scale,
                                           torch.empty((i1 - i0, 512), dtype=bf, device=dev), bias=bias)
         checks["items"] = i1 - i0
