@@ -1364,7 +1364,8 @@ __global__ void __launch_bounds__(kGvThreads * gv_groups(MT), gv_groups(MT) > 1 
 // stages it in shared memory ([128 columns][MP rows], padded against bank
 // conflicts), and after a cluster barrier CTA r sums the 8 columns
 // [8r, 8r + 8) across the cluster's shared memories (distributed shared
-// memory, int32 addition: exact in any order) and runs the epilogue for them.
+// memory, int32 addition: exact in any order), runs the epilogue on them and
+// writes each output row's 8 values with one 16-byte store.
 // One launch, no workspace; the weight streams through all clusters' SMs at
 // once.  No TMA load carries a multicast.
 namespace swp {
@@ -1374,12 +1375,16 @@ constexpr int kMaxStages = 16;
 constexpr int kMaxMP = 256;
 constexpr int W_BYTES = 128 * BK;  // weight rows of the tile
 constexpr int NUM_THREADS = 192;
-constexpr int kColsPerCta = 128 / kSplit;  // output columns each CTA reduces
+constexpr int kColsPerCta = 128 / kSplit;  // output columns each CTA reduces (8)
 // shared memory: a ring of stages of 16 KB of weight + MP x 128 B of A (as many
 // as fit, so that for small M every K block of the CTA is requested at once),
 // reused for the partial [128][MP + 4] int32 after the main loop
 constexpr int kRing = 192 * 1024;
-constexpr int SMEM_BYTES = kRing + 1024 + 256;
+// after the barriers: the epilogue's per-row activation scales (kMaxMP) and the
+// CTA's 8 columns' weight scales and bias, loaded while the main loop runs
+constexpr int kEpiBytes = (kMaxMP + 2 * 8) * 4;
+constexpr int kBarBytes = 512;  // full/empty[kMaxStages], tfull, TMEM address, abort flag (272 B)
+constexpr int SMEM_BYTES = kRing + 1024 + kBarBytes + kEpiBytes;
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
   asm volatile(
@@ -1428,6 +1433,43 @@ __device__ __forceinline__ void store_one(const EpiParams& ep, int64_t m, int64_
   }
 }
 
+// one output element's bits: the raw int32, or ((f32(acc) * sa) * sb) + bias
+// rounded to the output dtype (in the low bits for 16-bit dtypes)
+__device__ __forceinline__ int32_t out_bits(const EpiParams& ep, float sa, float sb, float bias, int64_t n,
+                                            int32_t acc) {
+  if (ep.out_dtype == RB_I32 || n >= ep.N) return acc;
+  float v = __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sb);
+  if (ep.bias != nullptr) v = __fadd_rn(v, bias);
+  if (ep.out_dtype == RB_F32) return __float_as_int(v);
+  if (ep.out_dtype == RB_BF16) return (int32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v));
+  return (int32_t)__half_as_ushort(__float2half_rn(v));
+}
+
+// the 8 staged outputs of row m, columns n0 .. n0+7 (n0 a multiple of 8): one
+// or two 16-byte stores when the row is whole and aligned, else one by one
+__device__ __forceinline__ void store_row8(const EpiParams& ep, int64_t m, int64_t n0, const int32_t* bits) {
+  const int esz = dtype_size(ep.out_dtype);
+  const int64_t o = m * ep.ldo + n0;
+  char* base = reinterpret_cast<char*>(ep.out) + o * esz;
+  const uint4 b0 = *reinterpret_cast<const uint4*>(bits), b1 = *reinterpret_cast<const uint4*>(bits + 4);
+  const bool vec = n0 + 8 <= ep.N && (reinterpret_cast<uintptr_t>(base) & 15) == 0;
+  if (esz == 4) {
+    if (vec) {
+      reinterpret_cast<uint4*>(base)[0] = b0;
+      reinterpret_cast<uint4*>(base)[1] = b1;
+    } else {
+      for (int j = 0; j < 8 && n0 + j < ep.N; ++j) reinterpret_cast<int32_t*>(base)[j] = bits[j];
+    }
+    return;
+  }
+  if (vec) {
+    *reinterpret_cast<uint4*>(base) = make_uint4((b0.x & 0xffffu) | (b0.y << 16), (b0.z & 0xffffu) | (b0.w << 16),
+                                                 (b1.x & 0xffffu) | (b1.y << 16), (b1.z & 0xffffu) | (b1.w << 16));
+  } else {
+    for (int j = 0; j < 8 && n0 + j < ep.N; ++j) reinterpret_cast<uint16_t*>(base)[j] = (uint16_t)bits[j];
+  }
+}
+
 // tmW: the weight [N, K] (128-row boxes); tmA: the activations [M, K] (MP-row boxes)
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     w8a8_gemm_swap_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
@@ -1443,6 +1485,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* tfull = empty + kMaxStages; // [1]           MMA -> epilogue
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_sa = reinterpret_cast<float*>(smem + kRing + kBarBytes);  // [mp] activation scale per row
+  float* s_sb = s_sa + kMaxMP;                                 // [8] weight scales of the CTA's columns
+  float* s_bias = s_sb + 8;                                    // [8] bias of the CTA's columns (0 without)
   int32_t* part = reinterpret_cast<int32_t*>(smem);  // after the main loop: [128][mp + 4]
   const int ldp = mp + 4;
 
@@ -1537,7 +1582,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!ok) *abort_flag = 1;
     }
   } else {
-    // --------------------------------------- TMEM -> shared partial [128][mp]
+    // ------------- epilogue operands into shared memory while the main loop runs
+    if (ep.out_dtype != RB_I32) {
+      const int et = threadIdx.x - 64;  // 0 .. 127
+      for (int m = et; m < (int)ep.M; m += 128) s_sa[m] = load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? m : 0);
+      if (et < 8) {
+        const int64_t n = n_tile0 + (int64_t)rank * kColsPerCta + et;
+        s_sb[et] = n < ep.N ? load_as_f32(ep.sb, ep.sb_dtype, n) : 0.0f;
+        s_bias[et] = (ep.bias != nullptr && n < ep.N) ? load_as_f32(ep.bias, ep.bias_dtype, n) : 0.0f;
+      }
+    }
+    // --------------------------------------- TMEM -> shared partial [128][ldp]
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane = output column of the tile
     bool ready = !has_k;
@@ -1561,7 +1616,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   pair::cluster_sync_all();  // every CTA's partial is in its shared memory
 
-  // ---- CTA `rank` sums columns [8 rank, 8 rank + 8) of the tile over the cluster
+  // ---- CTA `rank` sums columns [8 rank, 8 rank + 8) of the tile over the
+  // cluster (consecutive threads read consecutive rows of a column: each
+  // warp's remote reads are contiguous), applies the epilogue and stages the
+  // [M][8] outputs in its own shared memory, then writes one row's 8 outputs
+  // per thread (one 16-byte store for bf16 / f16)
+  int32_t* stage_out = part + 128 * ldp;  // [mp][8] raw output bits (int32 or the output dtype's)
+  const int64_t n0 = n_tile0 + (int64_t)rank * kColsPerCta;
   {
     const int m4n = (int)((ep.M + 3) / 4);     // groups of 4 rows of A that exist
     const int items = kColsPerCta * m4n;       // (column, 4 consecutive rows of A)
@@ -1582,15 +1643,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         acc.z += v[q].z;
         acc.w += v[q].w;
       }
-      const int64_t n = n_tile0 + col;
-      if (n < ep.N) {
-        const uint32_t a4[4] = {acc.x, acc.y, acc.z, acc.w};
+      const uint32_t a4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (m4 + i < ep.M) store_one(ep, m4 + i, n, (int32_t)a4[i]);
-      }
+      for (int i = 0; i < 4; ++i)
+        stage_out[(m4 + i) * kColsPerCta + j] = out_bits(ep, s_sa[m4 + i < ep.M ? m4 + i : 0], s_sb[j], s_bias[j],
+                                                         n0 + j, (int32_t)a4[i]);
     }
   }
+  __syncthreads();
+  for (int m = threadIdx.x; m < (int)ep.M; m += NUM_THREADS) store_row8(ep, m, n0, stage_out + m * kColsPerCta);
   pair::cluster_sync_all();  // no CTA leaves while another still reads its partial
   if (warp == 1) {
     tc_fence_after();
