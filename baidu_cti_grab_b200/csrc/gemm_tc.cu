@@ -768,7 +768,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // row (128 Welford chains of 4 elements, a shuffle-down merge of each group of
 // 32 chains, then groups {0,2}, {1,3} and the two halves), and writes
 // norm1(rep_emb) from a second read of TMEM.  The main loop waits for the
-// epilogue between tiles (one accumulator), a few percent of the tile time.
+// epilogue between tiles (one accumulator).  rb_w8a8_gemm_ln uses this kernel
+// below M = 4096; from there K2 + ln512_rows_kernel measured faster.
 struct LnParams {
   const void* gamma;
   const void* beta;
@@ -1966,6 +1967,97 @@ extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64
 // ----------------------------------------------------------------------------
 // K2 + the transformer's layer-0 LayerNorm(512): out as rb_w8a8_gemm, and
 // ln_out = LayerNorm(out) with gamma/beta (ATen's CUDA order, bit for bit).
+// ----------------------------------------------------------------------------
+// LayerNorm over rows of 512 in the order of ATen's CUDA LayerNorm for a
+// 512-wide row (128 threads, thread c a Welford chain over columns
+// 4c .. 4c+3; shuffle-down merge of each warp's 32 chains; warps {0,1} take
+// {2,3}, then warp 0 takes warp 1; rstd = rsqrtf(m2 / 512 + eps)), one warp per
+// row: lane l carries chains l, l + 32, l + 64, l + 96 (lane l of ATen's four
+// warps) as two packed pairs.  Used after K2 for the encoder's norm1 when the
+// separate pass is faster than the fused epilogue.
+namespace ln512 {
+constexpr int kRowsPerCta = 8;
+
+__device__ __forceinline__ void ld4(const void* p, int dtype, int64_t i, float* v) {
+  if (dtype == RB_F32) {
+    const float4 t = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  } else {
+    const uint2 t = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p) + i);
+    if (dtype == RB_BF16) {
+      v[0] = bf16_lo(t.x); v[1] = bf16_hi(t.x); v[2] = bf16_lo(t.y); v[3] = bf16_hi(t.y);
+    } else {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&t.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&t.y));
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void st4(void* p, int dtype, int64_t i, const float* v) {
+  if (dtype == RB_F32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i) = make_float4(v[0], v[1], v[2], v[3]);
+  } else if (dtype == RB_BF16) {
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p) + i) =
+        make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+  } else {
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p) + i) =
+        make_uint2(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]));
+  }
+}
+
+__global__ void __launch_bounds__(32 * kRowsPerCta)
+    ln512_rows_kernel(const void* x, int64_t ldx, int x_dtype, const void* gamma, const void* beta, int ln_dtype,
+                      float eps, void* y, int64_t ldy, int64_t M) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+  if (row >= M) return;
+  float v[4][4];  // [q][e]: column 4 (32 q + lane) + e, chain 32 q + lane
+#pragma unroll
+  for (int q = 0; q < 4; ++q) ld4(x, x_dtype, row * ldx + 4 * (32 * q + lane), v[q]);
+  Welford2 a{f2(0.0f, 0.0f), f2(0.0f, 0.0f)}, b = a;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float rc = 1.0f / (float)(e + 1);  // cuWelfordOnlineSum's 1 / (count + 1)
+    welford_push2(a, f2(v[0][e], v[2][e]), rc);
+    welford_push2(b, f2(v[1][e], v[3][e]), rc);
+  }
+  float cnt = 4.0f;
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) {
+    Welford2 oa, ob;
+    oa.mean.r = __shfl_down_sync(0xffffffffu, a.mean.r, d);
+    oa.m2.r = __shfl_down_sync(0xffffffffu, a.m2.r, d);
+    ob.mean.r = __shfl_down_sync(0xffffffffu, b.mean.r, d);
+    ob.m2.r = __shfl_down_sync(0xffffffffu, b.m2.r, d);
+    a = welford_merge2(a, oa, cnt);
+    b = welford_merge2(b, ob, cnt);
+    cnt = __fadd_rn(cnt, cnt);
+  }
+  float mean = 0.0f, rstd = 0.0f;
+  if (lane == 0) {
+    const float2 am = un(a.mean), aq = un(a.m2), bm = un(b.mean), bq = un(b.m2);
+    const float2 w02 = welford_merge1(am.x, aq.x, am.y, aq.y, cnt);  // cnt = 128
+    const float2 w13 = welford_merge1(bm.x, bq.x, bm.y, bq.y, cnt);
+    const float2 fin = welford_merge1(w02.x, w02.y, w13.x, w13.y, 256.0f);
+    mean = fin.x;
+    rstd = rsqrtf(__fadd_rn(__fdiv_rn(fin.y, 512.0f), eps));
+  }
+  mean = __shfl_sync(0xffffffffu, mean, 0);
+  rstd = __shfl_sync(0xffffffffu, rstd, 0);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int64_t c = 4 * (32 * q + lane);
+    float g[4], bb[4], o[4];
+    ld4(gamma, ln_dtype, c, g);
+    ld4(beta, ln_dtype, c, bb);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = __fmaf_rn(g[e], __fmul_rn(rstd, __fsub_rn(v[q][e], mean)), bb[e]);
+    st4(y, x_dtype, row * ldy + c, o);
+  }
+}
+}  // namespace ln512
+
 extern "C" int rb_w8a8_gemm_ln(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M, int64_t N,
                                int64_t K, const void* sa, int sa_dtype, int sa_per_row, const void* sb, int sb_dtype,
                                const void* bias, int bias_dtype, void* out, int64_t ldo, int out_dtype,
@@ -1993,6 +2085,20 @@ extern "C" int rb_w8a8_gemm_ln(const int8_t* A, int64_t lda, const int8_t* B, in
   if (!device_is_sm100()) return fail(RB_ERR_DEVICE, "rb_w8a8_gemm_ln needs an sm_100 (B200) device");
   if (!(K > 0 && K % 16 == 0 && lda % 16 == 0 && ldb % 16 == 0 && aligned(A, 16) && aligned(B, 16)))
     return fail(RB_ERR_UNSUPPORTED, "rb_w8a8_gemm_ln needs K %% 16 == 0 and 16-byte aligned operand rows");
+  // From M = 4096 (the CTA-pair GEMM, no workspace) K2 followed by a separate
+  // LayerNorm(512) pass over its output, still in L2, is faster than the fused
+  // epilogue (0.62 against 0.70 ms at M = 103k on a B200: the 512-column tiles
+  // of the fused kernel fill fewer waves and its tensor pipe idles while the
+  // epilogue runs); both give the same bits.
+  if (M >= RB_GEMM_PAIR_MIN_M && aligned(ln_out, 16) && (ldl * dtype_size(out_dtype)) % 16 == 0) {
+    int rc2 = rb_w8a8_gemm_ws(A, lda, B, ldb, M, N, K, sa, sa_dtype, sa_per_row, sb, sb_dtype, bias, bias_dtype, out,
+                              ldo, out_dtype, nullptr, 0, stream);
+    if (rc2) return rc2;
+    const unsigned blocks = (unsigned)((M + ln512::kRowsPerCta - 1) / ln512::kRowsPerCta);
+    ln512::ln512_rows_kernel<<<blocks, 32 * ln512::kRowsPerCta, 0, (cudaStream_t)stream>>>(
+        out, ldo, out_dtype, ln_gamma, ln_beta, ln_dtype, eps, ln_out, ldl, M);
+    return check_cuda(cudaGetLastError(), "ln512_rows_kernel launch");
+  }
   EpiParams ep{};
   ep.sa = sa;
   ep.sb = sb;

@@ -1,7 +1,9 @@
 """K2 with the transformer's first LayerNorm fused (rb_w8a8_gemm_ln) on the GPU.
 
 models.py:216-217 begins layer 0 of the encoder with ``residual = x;
-x = norm1[0](x)`` on the RepEncoder output.  The fused kernel returns both:
+x = norm1[0](x)`` on the RepEncoder output.  rb_w8a8_gemm_ln returns both
+(below M = 4096 from one kernel with the LayerNorm in the GEMM's epilogue,
+from M = 4096 as K2 followed by a LayerNorm(512) pass over its output):
 ``out`` must equal rb_w8a8_gemm's result and ``ln_out`` ATen's CUDA
 LayerNorm(512) of ``out``, bit for bit (and the oracle's restatement of that
 LayerNorm, given the GPU's rsqrtf for rstd).
@@ -17,7 +19,8 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("M,static,out_dtype", [(1, False, "bfloat16"), (100, False, "bfloat16"),
                                                 (256, True, "bfloat16"), (1000, False, "float32"),
-                                                (4099, False, "bfloat16"), (20000, False, "bfloat16")])
+                                                (4099, False, "bfloat16"), (20000, False, "bfloat16"),
+                                                (8192, True, "float32")])
 def test_gemm_ln_matches_gemm_then_aten_layernorm(cuda_device, M, static, out_dtype):
     import torch
     import torch.nn.functional as F
