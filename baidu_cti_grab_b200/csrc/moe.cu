@@ -423,15 +423,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t r[32];
         tc::tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
         if (!live) continue;
+        // the chunk's 32 bias values: four 16-byte loads when aligned
+        T bv[32];
+        if (bias != nullptr) {
+          const T* bp = bias + (int64_t)e * p.N + col0;
+          if ((reinterpret_cast<uintptr_t>(bp) & 15) == 0 && col0 + 32 <= p.N) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(bv + 8 * q) = reinterpret_cast<const uint4*>(bp)[q];
+          } else {
+#pragma unroll
+            for (int q = 0; q < 32; ++q) bv[q] = col0 + q < p.N ? bp[q] : T(0.0f);
+          }
+        }
         uint32_t packed[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           float v2[2];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int col = col0 + 2 * j + h;
             float v = round_to<T>(__uint_as_float(r[2 * j + h]));
-            if (bias != nullptr) v = round_to<T>(__fadd_rn(v, (float)bias[(int64_t)e * p.N + col]));
+            if (bias != nullptr) v = round_to<T>(__fadd_rn(v, (float)bv[2 * j + h]));
             if (EPI == 1) {
               v = v < 0.0f ? 0.0f : v;
             } else {
