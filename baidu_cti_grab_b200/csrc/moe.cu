@@ -33,6 +33,8 @@
 // from cuBLAS's.
 #include "common.cuh"
 
+#include <type_traits>
+
 namespace rb {
 namespace moe {
 
@@ -436,6 +438,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
         uint32_t packed[16];
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+          if (bias != nullptr) {
+            // bf16 with bias, pairs of columns: the bmm result rounded (one
+            // cvt for both), widened, + bias as the bf16 operand of a mixed
+            // fp32 add, then (1) relu before the rounding -- exact here: a sum
+            // of two bf16 values is 0, -0 or at least 2^-133 in magnitude, so
+            // it is negative exactly when its rounding is -- or (2) rounded,
+            // widened, times the score and rounded; one cvt packs each pair
+            const uint32_t* bw = reinterpret_cast<const uint32_t*>(bv);
+            const F2 w2 = f2(w, w);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const uint32_t p1 = pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+              float lo = add_lo(bf16_lo(p1), bw[j]), hi = add_hi(bf16_hi(p1), bw[j]);
+              if (EPI == 1) {
+                lo = lo < 0.0f ? 0.0f : lo;
+                hi = hi < 0.0f ? 0.0f : hi;
+                packed[j] = pack_bf16x2(lo, hi);
+              } else {
+                const uint32_t p2 = pack_bf16x2(lo, hi);
+                const float2 v = un(mul2v(f2(bf16_lo(p2), bf16_hi(p2)), w2));
+                packed[j] = pack_bf16x2(v.x, v.y);
+              }
+            }
+            T* dst = reinterpret_cast<T*>(p.out) + orow * p.ldo + col0;
+            stg_v8(dst, packed);
+            stg_v8(dst + 16, packed + 8);
+            continue;
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           float v2[2];
