@@ -33,7 +33,9 @@ constexpr int kMaxWarps = (RB_MAX_SLOTS + kSlotsPerWarp - 1) / kSlotsPerWarp;
 #endif
 constexpr int kDim = 512;
 
-enum RepMode : int { kGatherLnQuant = 0, kGatherPool = 1, kDenseLnQuant = 2 };
+// kGatherLnQuantPlain: kGatherLnQuant with dynamic quantisation and no pooled or
+// LayerNorm output (the RepEncoder forward), its runtime options compiled out
+enum RepMode : int { kGatherLnQuant = 0, kGatherPool = 1, kDenseLnQuant = 2, kGatherLnQuantPlain = 3 };
 
 struct SlotArgs {
   // ids and offsets of each slot: int64, or int32 for the kernels instantiated
@@ -352,7 +354,9 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int64_t item = p.item_shift == 0 ? (int64_t)blockIdx.x : ((int64_t)blockIdx.x + p.item_shift) % p.num_items;
+  constexpr bool kPlain = MODE == kGatherLnQuantPlain;
+  const int64_t item =
+      (kPlain || p.item_shift == 0) ? (int64_t)blockIdx.x : ((int64_t)blockIdx.x + p.item_shift) % p.num_items;
   // kS: the slot count when known at compile time (28 for the RepEncoder), else 0
   const int S = kS ? kS : p.num_slots;
   // warp w owns slots 4w .. 4w+3 (fewer in the last warp when S % 4 != 0)
@@ -383,7 +387,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       st_words(s_words + s * 256, lane, w);
       if constexpr (MODE == kGatherPool) {
         if (p.num_dest == 0) st_words(out_row + (int64_t)p.slots.col_slot[s] * kDim, lane, w);
-      } else if (p.pooled != nullptr) {
+      } else if (!kPlain && p.pooled != nullptr) {
         st_words(reinterpret_cast<T*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, w);
       }
     } else {
@@ -393,7 +397,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       sts_pairs(s_f32, s, lane, x);
       if constexpr (MODE == kGatherPool) {
         stg_pairs(reinterpret_cast<float*>(out_row) + (int64_t)p.slots.col_slot[s] * kDim, lane, x);
-      } else if (p.pooled != nullptr) {
+      } else if (!kPlain && p.pooled != nullptr) {
         stg_pairs(reinterpret_cast<float*>(p.pooled) + item * p.ldp + (int64_t)s * kDim, lane, x);
       }
     }
@@ -635,7 +639,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
           w[i] = pack_bf16x2(v.x, v.y);
         }
         st_words(s_words + s * 256, lane, w);
-        if (p.ln != nullptr) st_words(reinterpret_cast<T*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, w);
+        if (!kPlain && p.ln != nullptr) st_words(reinterpret_cast<T*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, w);
       } else {
         F2 x[8], y[8];
         lds_pairs(s_f32, s, lane, x);
@@ -643,7 +647,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
         for (int i = 0; i < 8; ++i)
           y[i] = fma2(mul2(rstd2, sub2(x[i], mean2)), aff.gamma(i, bf_affine), aff.beta(i, bf_affine));
         sts_pairs(s_f32, s, lane, y);
-        if (p.ln != nullptr) stg_pairs(reinterpret_cast<float*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, y);
+        if (!kPlain && p.ln != nullptr) stg_pairs(reinterpret_cast<float*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, y);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float2 v = un(y[i]);
@@ -651,14 +655,14 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
         }
       }
     }
-    if (p.act_mode == RB_ACT_NONE) return;
+    if (!kPlain && p.act_mode == RB_ACT_NONE) return;
     if constexpr (kBf16) amax = round_bf16(amax);
     amax = warp_max(amax);
     if (lane == 0) s_wmax[warp] = amax;
     __syncthreads();
     // every thread derives the quantiser scale (no further barrier)
     float inv;
-    if (p.act_mode == RB_ACT_DYNAMIC) {
+    if (kPlain || p.act_mode == RB_ACT_DYNAMIC) {
       float m = 0.0f;
       for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, s_wmax[w]);
       m = fmaxf(m, 1e-8f);
@@ -669,7 +673,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     }
     const F2 inv2 = f2(inv, inv);
     int8_t* const q_lane = p.q + item * p.ldq + 8 * lane;  // this lane's columns of the item's int8 row
-    const bool clamp = p.act_mode == RB_ACT_STATIC;
+    const bool clamp = !kPlain && p.act_mode == RB_ACT_STATIC;
     // ---- int8 = clamp(round_half_away(y * inv), -128, 127)
 #pragma unroll
     for (int j = 0; j < kSlotsPerWarp; ++j) {
@@ -835,6 +839,9 @@ static int gather_ln_quant(const void* table, int table_dtype, int64_t num_rows,
   p.pooled = pooled_out;
   p.ldp = (int64_t)num_slots * kDim;
   p.ln = ln_out;
+  if (pooled_out == nullptr && ln_out == nullptr && act_mode == RB_ACT_DYNAMIC)
+    return index_dtype == RB_I32 ? launch_rep<kGatherLnQuantPlain, int32_t>(p, table_dtype, (cudaStream_t)stream)
+                                 : launch_rep<kGatherLnQuantPlain, int64_t>(p, table_dtype, (cudaStream_t)stream);
   return index_dtype == RB_I32 ? launch_rep<kGatherLnQuant, int32_t>(p, table_dtype, (cudaStream_t)stream)
                                : launch_rep<kGatherLnQuant, int64_t>(p, table_dtype, (cudaStream_t)stream);
 }
