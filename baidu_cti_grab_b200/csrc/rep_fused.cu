@@ -620,8 +620,9 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     const F2 mean2 = f2(mean, mean);
     const F2 rstd2 = f2(rstd, rstd);
     // ---- y = fma(rstd * (x - mean), gamma, beta) rounded to T, in place; absmax
+    // (a rolled loop: the smaller code measured 2 % faster than four copies)
     float amax = 0.0f;
-#pragma unroll
+#pragma unroll 1
     for (int j = 0; j < kSlotsPerWarp; ++j) {
       if (j >= nsl) break;
       const int s = slot_of(j);
