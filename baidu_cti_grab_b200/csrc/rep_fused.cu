@@ -33,9 +33,16 @@ constexpr int kMaxWarps = (RB_MAX_SLOTS + kSlotsPerWarp - 1) / kSlotsPerWarp;
 #endif
 constexpr int kDim = 512;
 
-// kGatherLnQuantPlain: kGatherLnQuant with dynamic quantisation and no pooled or
-// LayerNorm output (the RepEncoder forward), its runtime options compiled out
-enum RepMode : int { kGatherLnQuant = 0, kGatherPool = 1, kDenseLnQuant = 2, kGatherLnQuantPlain = 3 };
+// kGatherLnQuantPlain / kDenseLnQuantPlain: kGatherLnQuant / kDenseLnQuant with
+// dynamic quantisation and no pooled or LayerNorm output (the RepEncoder forward
+// and the slot-sharded path's second stage), their runtime options compiled out
+enum RepMode : int {
+  kGatherLnQuant = 0,
+  kGatherPool = 1,
+  kDenseLnQuant = 2,
+  kGatherLnQuantPlain = 3,
+  kDenseLnQuantPlain = 4
+};
 
 struct SlotArgs {
   // ids and offsets of each slot: int64, or int32 for the kernels instantiated
@@ -354,7 +361,8 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  constexpr bool kPlain = MODE == kGatherLnQuantPlain;
+  constexpr bool kPlain = MODE == kGatherLnQuantPlain || MODE == kDenseLnQuantPlain;
+  constexpr bool kDense = MODE == kDenseLnQuant || MODE == kDenseLnQuantPlain;
   const int64_t item =
       (kPlain || p.item_shift == 0) ? (int64_t)blockIdx.x : ((int64_t)blockIdx.x + p.item_shift) % p.num_items;
   // kS: the slot count when known at compile time (28 for the RepEncoder), else 0
@@ -403,7 +411,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     }
   };
 
-  if constexpr (MODE == kDenseLnQuant) {
+  if constexpr (kDense) {
 #pragma unroll
     for (int j = 0; j < kSlotsPerWarp; ++j) {
       if (j >= nsl) break;
@@ -984,6 +992,7 @@ static int layernorm_quant_common(RepParams& p, int x_dtype, int64_t num_items, 
   p.ldq = ldq;
   p.scale = scale_out;
   p.ln = ln_out;
+  if (ln_out == nullptr && act_mode == RB_ACT_DYNAMIC) return launch_rep<kDenseLnQuantPlain>(p, x_dtype, (cudaStream_t)stream);
   return launch_rep<kDenseLnQuant>(p, x_dtype, (cudaStream_t)stream);
 }
 
