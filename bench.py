@@ -744,6 +744,38 @@ def b200_arm(args):
                          "kernel, against rb_w8a8_gemm + F.layer_norm on the same operands"}
         del ln_buf
 
+    # ---- the path infer.py takes: the module forward on the reference's collate
+    # output left on the host (int64 CPU tensors per slot), i.e. one staged H2D
+    # copy of the ids/offsets, K1 and K2 per call, rep_emb left on the device for
+    # the transformer (rank 0, wall clock over the calls, the device drained at
+    # the end)
+    ref_layout = None
+    if world == 1 and not args.no_e2e:
+        import torch as _t
+        cpu_batches = []
+        for b in host_batches:
+            cb = {"user_offsets": _t.from_numpy(np.asarray(b["user_offsets"], dtype=np.int64))}
+            for s in range(1, 29):
+                cb[s] = [_t.from_numpy(np.asarray(b[s][0], dtype=np.int64)),
+                         _t.from_numpy(np.asarray(b[s][1], dtype=np.int64))]
+            cpu_batches.append(cb)
+        with torch.no_grad():
+            for i in range(3):
+                rep(cpu_batches[i % len(cpu_batches)])
+            torch.cuda.synchronize()
+            nref = 20
+            t0 = time.perf_counter()
+            for i in range(nref):
+                rep(cpu_batches[i % len(cpu_batches)])
+            torch.cuda.synchronize()
+            ref_wall = time.perf_counter() - t0
+        ref_items = sum(stats[i % len(stats)][0] for i in range(nref))
+        ref_layout = {"value": round(ref_items / ref_wall, 1), "unit": "items/s", "calls": nref,
+                      "ms_per_call": round(ref_wall / nref * 1e3, 4),
+                      "what": "RepEncoder.forward (fuse_mode b200) on the reference's collate batch left on the host "
+                              "(int64 CPU values/offsets per slot, as models.py:31 receives them): one staged pinned "
+                              "H2D copy, K1, K2; rep_emb stays on the device for the encoder; wall clock"}
+
     # ---- e2e through the public API from pinned host memory: packed host
     # batches, H2D / forward / D2H of successive batches overlapped on streams
     e2e = None
@@ -877,6 +909,8 @@ def b200_arm(args):
             line["kernels"]["smoe"] = smoe
         if k2_ln is not None:
             line["kernels"]["k2_ln"] = k2_ln
+        if ref_layout is not None:
+            line["reference_layout_forward"] = ref_layout
 
     # ---- CPU baseline (rank 0, N=1 only)
     if world > 1:
