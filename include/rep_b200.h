@@ -233,9 +233,12 @@ int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, 
                     int32_t* workspace, int64_t workspace_elems, void* stream);
 
 /*
- * rb_w8a8_gemm with the transformer's first LayerNorm fused into the epilogue
+ * rb_w8a8_gemm together with the transformer's first LayerNorm
  * (models.py:216-217: layer 0 begins residual = x; x = norm1[0](x), x being
- * the RepEncoder output this GEMM produces).  out is rb_w8a8_gemm's result
+ * the RepEncoder output this GEMM produces): below M = 4096 one kernel with the
+ * LayerNorm in the GEMM's epilogue, from M = 4096 the GEMM followed by a
+ * LayerNorm pass over its output on the same stream (measured faster there;
+ * the bits are the same either way).  out is rb_w8a8_gemm's result
  * (the residual), ln_out = LayerNorm(out) over the 512 columns with
  * ln_gamma/ln_beta (ln_dtype RB_F32/RB_BF16/RB_F16) and eps, in the reduction
  * order of ATen's CUDA LayerNorm, so it equals nn.LayerNorm on out bit for
