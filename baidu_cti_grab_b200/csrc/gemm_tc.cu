@@ -51,16 +51,17 @@
 // M range of the swapped-operand cluster kernel (the weight as the MMA's 128-row
 // operand, the activation rows as its N, K split over a 16-CTA cluster).  Its
 // fixed cost (cluster launch, TMEM, two cluster barriers, the DSMEM sum) is
-// about 3.9 us on a B200, so the dp4a GEMV keeps M <= RB_GEMV_MAX_M, and above
-// 128 rows the split one-SM kernel is faster again (K = 14336, N = 512:
-// M = 17 / 64 / 128 take 8.4 / 9.5 / 12.3 us against 10.8 / 12.0 / 14.5 us
-// split; M = 256 16.5 against 15.1 us).
+// several us on a B200, so the dp4a GEMV keeps M <= RB_GEMV_MAX_M; up to 256
+// rows (the MMA's largest N) it beats the split one-SM kernel (K = 14336,
+// N = 512: M = 17 / 64 / 128 / 192 / 256 take 7.4 / 8.5 / 10.6 / 12.7 / 14.6 us
+// against 10.8 / 12.0 / 14.5 / 14.9 / 15.2 us split).
 #ifndef RB_GEMV_MAX_M
 #define RB_GEMV_MAX_M 16
 #endif
 #ifndef RB_GEMM_SWAP_MAX_M
-#define RB_GEMM_SWAP_MAX_M 128
+#define RB_GEMM_SWAP_MAX_M 256
 #endif
+static_assert(RB_GEMM_SWAP_MAX_M <= 256, "the swapped kernel's N side holds at most 256 activation rows");
 
 namespace rb {
 namespace tc {

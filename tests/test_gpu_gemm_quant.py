@@ -51,6 +51,8 @@ def test_gemm_golden(cuda_device):
                                    (300, 592, 48), (1000, 14336, 512), (257, 128, 300), (64, 16, 256),
                                    (4096, 14336, 512), (33, 14336, 200), (1024, 14336, 512), (1025, 592, 300),
                                    (3000, 1024, 48), (2048, 14336, 257),
+                                   # swapped operands up to M = 256 (the MMA's N side)
+                                   (200, 14336, 512), (256, 14336, 520), (250, 592, 300), (160, 4096, 40),
                                    # M <= 16: one 16-byte K chunk, K over one round of
                                    # 128 chunks per CTA, column counts off the 16-column groups
                                    (3, 16, 48), (16, 16400, 40), (9, 2064, 17), (2, 14336, 1),
