@@ -22,9 +22,11 @@
 //               dequant + bias in fp32, vector stores; releases the TMEM
 //               buffer so the MMA warp overlaps the next tile's main loop.
 // For M >= RB_GEMM_PAIR_MIN_M a two-SM variant (namespace pair) runs each
-// 256x256 tile on a cluster of two CTAs with tcgen05.mma.cta_group::2; for
-// 17 <= M with fewer tiles than SMs the one-SM kernel splits K across CTAs
-// into an int32 workspace that splitk_finalize_kernel sums in split order; for
+// 256x256 tile on a cluster of two CTAs with tcgen05.mma.cta_group::2; with
+// fewer tiles than half the pairs (from M = RB_GEMM_PAIR_SPLIT_MIN_M when the
+// caller gives a workspace) it splits each tile's K range over pairs, and for
+// smaller M with fewer tiles than SMs the one-SM kernel splits K across CTAs;
+// both write int32 partials that splitk_finalize_kernel sums; for
 // M <= 16 w8a8_gemv_kernel uses dp4a on the CUDA cores in clusters of 8 CTAs
 // split along K, whose partial sums meet in the leader's shared memory.  No
 // TMA load carries a cluster multicast (only tcgen05.commit signals both CTAs
@@ -47,6 +49,14 @@
 // one-SM kernel, split along K, spreads the work over all SMs.
 #ifndef RB_GEMM_PAIR_MIN_M
 #define RB_GEMM_PAIR_MIN_M 4096
+#endif
+// With a split-K workspace the two-SM kernel takes over from M = 2048: its
+// 256 x 256 tiles split along K over the pairs beat the split one-SM kernel
+// (K = 14336, N = 512 on a B200: M = 2048 / 3072 / 4096 in 24.9 / 30.3 /
+// 34.5 us against 25.9 / 31.7 us split one-SM and 43.5 us unsplit pairs; at
+// M = 1024 the one-SM split is ahead, 20.5 against 20.9 us).
+#ifndef RB_GEMM_PAIR_SPLIT_MIN_M
+#define RB_GEMM_PAIR_SPLIT_MIN_M 2048
 #endif
 // M range of the swapped-operand cluster kernel (the weight as the MMA's 128-row
 // operand, the activation rows as its N, K split over a 16-CTA cluster).  Its
@@ -640,8 +650,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int64_t m_tiles = (ep.M + BM - 1) / BM;
   const int64_t n_tiles = (ep.N + BN - 1) / BN;
-  const int64_t num_tiles = m_tiles * n_tiles;
+  const int ksplits = ep.ksplits;
+  // work unit t: K split t % ksplits of output tile t / ksplits (the splits of
+  // one tile run on neighbouring pairs); split s covers k blocks
+  // [s*kblocks/ksplits, (s+1)*kblocks/ksplits), at least two of them
+  const int64_t num_tiles = m_tiles * n_tiles * ksplits;
   const int kblocks = (int)((ep.K + BK - 1) / BK);
+  auto kb_begin = [&](int64_t t) { return (int)((t % ksplits) * kblocks / ksplits); };
+  auto kb_end = [&](int64_t t) { return (int)((t % ksplits + 1) * kblocks / ksplits); };
+  auto tile_mi = [&](int64_t t) { return (t / ksplits) / n_tiles; };
+  auto tile_ni = [&](int64_t t) { return (t / ksplits) % n_tiles; };
   const int64_t pair_id = blockIdx.x >> 1;
   const int64_t num_pairs = gridDim.x >> 1;
 
@@ -653,9 +671,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0, issued = 0, issued_phase = 0;
       bool ok = true;
       for (int64_t tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
-        const int m0 = (int)((tile / n_tiles) * BM) + (int)rank * 128;
-        const int n0 = (int)((tile % n_tiles) * BN) + (int)rank * (BN / 2);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int m0 = (int)(tile_mi(tile) * BM) + (int)rank * 128;
+        const int n0 = (int)(tile_ni(tile) * BN) + (int)rank * (BN / 2);
+        const int kb1 = kb_end(tile);
+        for (int kb = kb_begin(tile); kb < kb1; ++kb) {
           if (!mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, kWaitTimeoutProducer, abort_flag)) {
             ok = false;
             break;
@@ -690,7 +709,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!mbar_wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1, kWaitTimeoutMma, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int kb0 = kb_begin(tile), kb1 = kb_end(tile);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(smem_u32(&full[stage]), phase, kWaitTimeoutMma, abort_flag)) {
             ok = false;
             break;
@@ -701,7 +721,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / MMA_K; ++k)
             umma_i8_pair(d_tmem, adesc + (uint64_t)(k * MMA_K / 16), bdesc + (uint64_t)(k * MMA_K / 16), C::IDESC,
-                         (kb > 0 || k > 0) ? 1u : 0u);
+                         (kb > kb0 || k > 0) ? 1u : 0u);
           umma_commit_both(smem_u32(&empty[stage]));
           if (++stage == STAGES) {
             stage = 0;
@@ -725,21 +745,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t tempty_leader1 = map_rank(smem_u32(&tempty[1]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
+    // split-K units store raw int32 partials into their split's [M, N] slab
+    EpiParams pep = ep;
+    pep.out_dtype = RB_I32;
+    pep.ldo = ep.N;
     for (int64_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
-      const int64_t m0 = (tile / n_tiles) * BM + (int64_t)rank * 128;
-      const int64_t n0 = (tile % n_tiles) * BN;
+      const int64_t m0 = tile_mi(tile) * BM + (int64_t)rank * 128;
+      const int64_t n0 = tile_ni(tile) * BN;
       if (!mbar_wait_bounded(smem_u32(&tfull[acc]), acc_phase, kWaitTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const int64_t row = m0 + quarter * 32 + lane;
       float sa_v = 0.0f;
-      if (row < ep.M && ep.out_dtype != RB_I32) sa_v = load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? row : 0);
+      if (row < ep.M && ep.out_dtype != RB_I32 && ksplits == 1)
+        sa_v = load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? row : 0);
+      if (ksplits > 1) pep.out = ep.partials + (tile % ksplits) * ep.M * ep.N;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int64_t col0 = n0 + c * 32;
         if (col0 >= ep.N) break;  // warp-uniform
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-        if (row < ep.M) epilogue_32(r, row, col0, sa_v, ep);
+        if (row < ep.M) epilogue_32(r, row, col0, sa_v, ksplits > 1 ? pep : ep);
       }
       tc_fence_before();
       __syncwarp();
@@ -1125,34 +1151,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 }  // namespace pair
 
-// Split-K reduction: out[m,n] = epilogue(sum over splits s = 0..S-1 of the int32
-// partials, in split order).  int32 addition is exact, so the result equals the
-// unsplit GEMM's bit for bit.
-__global__ void splitk_finalize_kernel(const __grid_constant__ EpiParams ep) {
-  const int64_t total = ep.M * ep.N;
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    int32_t acc = 0;
-    for (int s = 0; s < ep.ksplits; ++s) acc += ep.partials[s * total + idx];
-    const int64_t m = idx / ep.N, n = idx % ep.N;
-    if (ep.out_dtype == RB_I32) {
-      reinterpret_cast<int32_t*>(ep.out)[m * ep.ldo + n] = acc;
-      continue;
-    }
-    float v = __int2float_rn(acc);
-    v = __fmul_rn(v, load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? m : 0));
-    v = __fmul_rn(v, load_as_f32(ep.sb, ep.sb_dtype, n));
-    if (ep.bias != nullptr) v = __fadd_rn(v, load_as_f32(ep.bias, ep.bias_dtype, n));
-    if (ep.out_dtype == RB_F32) {
-      reinterpret_cast<float*>(ep.out)[m * ep.ldo + n] = v;
-    } else if (ep.out_dtype == RB_BF16) {
-      reinterpret_cast<__nv_bfloat16*>(ep.out)[m * ep.ldo + n] = __float2bfloat16_rn(v);
-    } else {
-      reinterpret_cast<__half*>(ep.out)[m * ep.ldo + n] = __float2half_rn(v);
-    }
-  }
-}
-
 // out[m, n] = epilogue(acc) for one element (the finalize and small-M paths)
 __device__ __forceinline__ void epilogue_one(int32_t acc, int64_t m, int64_t n, const EpiParams& ep) {
   if (ep.out_dtype == RB_I32) {
@@ -1169,6 +1167,84 @@ __device__ __forceinline__ void epilogue_one(int32_t acc, int64_t m, int64_t n, 
     reinterpret_cast<__nv_bfloat16*>(ep.out)[m * ep.ldo + n] = __float2bfloat16_rn(v);
   } else {
     reinterpret_cast<__half*>(ep.out)[m * ep.ldo + n] = __float2half_rn(v);
+  }
+}
+
+// Split-K reduction: out[m, n] = epilogue(sum over the splits of the int32
+// partials).  int32 addition is exact (modulo 2^32, in any order), so the
+// result equals the unsplit GEMM's bit for bit.  A thread owns 4 consecutive
+// columns of one row: one 16-byte load per split (four splits in flight), the
+// scales and bias as 4-wide vectors and one store; the epilogue's fp32 steps
+// are the GEMM kernels' ((acc * sa) * sb) + bias, one rounded op at a time.
+// Ragged or unaligned groups go element by element.
+constexpr int kFinCols = 4;
+
+__device__ __forceinline__ void ld_param4(const void* p, int dtype, int64_t i, float* out) {
+  if (dtype == RB_F32) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i));
+    out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+    return;
+  }
+  const uint2 w = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p) + i));
+  if (dtype == RB_BF16) {
+    out[0] = bf16_lo(w.x); out[1] = bf16_hi(w.x); out[2] = bf16_lo(w.y); out[3] = bf16_hi(w.y);
+  } else {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+    out[0] = a.x; out[1] = a.y; out[2] = b.x; out[3] = b.y;
+  }
+}
+
+__global__ void __launch_bounds__(256) splitk_finalize_kernel(const __grid_constant__ EpiParams ep) {
+  const uint64_t groups = (uint64_t)((ep.N + kFinCols - 1) / kFinCols);  // column groups per row
+  const uint64_t total = (uint64_t)ep.M * groups;
+  const int64_t slab = ep.M * ep.N;
+  const size_t osz = ep.out_dtype == RB_F32 || ep.out_dtype == RB_I32 ? 4 : 2;
+  const bool vec_in = ep.N % 4 == 0 && aligned(ep.partials, 16);
+  const bool vec_par = ep.out_dtype == RB_I32 ||
+                       (aligned(ep.sb, 16) && (ep.bias == nullptr || aligned(ep.bias, 16)));
+  const bool vec_out = aligned(ep.out, 16) && (ep.ldo * (int64_t)osz) % 16 == 0;
+  for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (uint64_t)gridDim.x * blockDim.x) {
+    const int64_t m = (int64_t)(t / groups);
+    const int64_t n0 = (int64_t)(t % groups) * kFinCols;
+    if (!(vec_in && vec_par && vec_out && n0 + kFinCols <= ep.N)) {
+      for (int j = 0; j < kFinCols && n0 + j < ep.N; ++j) {
+        int32_t acc = 0;
+        for (int s = 0; s < ep.ksplits; ++s) acc += ep.partials[s * slab + m * ep.N + n0 + j];
+        epilogue_one(acc, m, n0 + j, ep);
+      }
+      continue;
+    }
+    uint32_t a[4] = {0u, 0u, 0u, 0u};
+    const uint4* src = reinterpret_cast<const uint4*>(ep.partials + m * ep.N + n0);
+#pragma unroll 4
+    for (int s = 0; s < ep.ksplits; ++s) {
+      const uint4 x = __ldcs(src + s * (slab / 4));
+      a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
+    }
+    if (ep.out_dtype == RB_I32) {
+      *reinterpret_cast<uint4*>(reinterpret_cast<int32_t*>(ep.out) + m * ep.ldo + n0) = make_uint4(a[0], a[1], a[2], a[3]);
+      continue;
+    }
+    const float sa_v = load_as_f32(ep.sa, ep.sa_dtype, ep.sa_per_row ? m : 0);
+    float sb[4], bi[4];
+    ld_param4(ep.sb, ep.sb_dtype, n0, sb);
+    if (ep.bias != nullptr) ld_param4(ep.bias, ep.bias_dtype, n0, bi);
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[k] = __fmul_rn(__fmul_rn(__int2float_rn((int)a[k]), sa_v), sb[k]);
+      if (ep.bias != nullptr) v[k] = __fadd_rn(v[k], bi[k]);
+    }
+    if (ep.out_dtype == RB_F32) {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(ep.out) + m * ep.ldo + n0) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      const bool bf = ep.out_dtype == RB_BF16;
+      const uint32_t w0 = bf ? pack_bf16x2(v[0], v[1]) : pack_f16x2(v[0], v[1]);
+      const uint32_t w1 = bf ? pack_bf16x2(v[2], v[3]) : pack_f16x2(v[2], v[3]);
+      *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(ep.out) + m * ep.ldo + n0) = make_uint2(w0, w1);
+    }
   }
 }
 
@@ -1755,6 +1831,14 @@ static std::once_flag g_ln_attr_once[64];
 
 using namespace rb;
 
+// the split-K reduction over M x ceil(N / 4) column groups, one per thread
+static int launch_splitk_finalize(const rb::tc::EpiParams& ep, cudaStream_t st) {
+  const int64_t groups = ep.M * ((ep.N + rb::tc::kFinCols - 1) / rb::tc::kFinCols);
+  const int64_t blocks = std::min<int64_t>((groups + 255) / 256, (int64_t)sm_count() * 16);
+  rb::tc::splitk_finalize_kernel<<<(unsigned)blocks, 256, 0, st>>>(ep);
+  return check_cuda(cudaGetLastError(), "splitk_finalize_kernel launch");
+}
+
 // split-K factor for the one-SM kernel (1 = no split): enough (m, n, k) tiles to
 // cover the SMs, at least two K blocks per split, and at most kMaxKSplits: every
 // split writes and the finalize reads back an M x N int32 partial, which past
@@ -1772,9 +1856,25 @@ static int choose_ksplits(int64_t M, int64_t N, int64_t K) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(s, kMaxKSplits));
 }
 
+// split-K factor for the two-SM kernel: when the 256 x 256 tiles cover at most
+// half of the CTA pairs, each tile's K range is split over pairs (int32
+// partials summed by splitk_finalize_kernel).  Then ksplits * M * N <=
+// pairs * 256 * 256 int32, the same bound as the one-SM kernel's split.
+static int choose_pair_ksplits(int64_t M, int64_t N, int64_t K) {
+  using namespace rb::tc;
+  if (M < RB_GEMM_PAIR_SPLIT_MIN_M || K <= 0 || K % 16 != 0) return 1;
+  const int64_t pairs = sm_count() / 2;
+  const int64_t t256 = ((M + 255) / 256) * ((N + 255) / 256);
+  const int64_t kblocks = (K + pair::BK - 1) / pair::BK;
+  if (2 * t256 > pairs) return 1;
+  const int64_t s = std::min<int64_t>(std::min<int64_t>(pairs / t256, kblocks / 2), kMaxKSplits);
+  return (int)std::max<int64_t>(1, s);
+}
+
 extern "C" int64_t rb_w8a8_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0) return 0;
-  const int s = choose_ksplits(M, N, K);
+  const int pks = choose_pair_ksplits(M, N, K);
+  const int s = (M >= RB_GEMM_PAIR_MIN_M || pks > 1) ? pks : choose_ksplits(M, N, K);
   return s > 1 ? (int64_t)s * M * N : 0;
 }
 
@@ -1879,7 +1979,10 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
     return check_cuda(cudaLaunchKernelEx(&cfg, swp::w8a8_gemm_swap_kernel, tmW, tmAct, ep, mp),
                       "w8a8_gemm_swap_kernel launch");
   }
-  if (M >= RB_GEMM_PAIR_MIN_M) {
+  // the two-SM kernel split along K (needs the workspace) from M = RB_GEMM_PAIR_SPLIT_MIN_M
+  int pks = choose_pair_ksplits(M, N, K);
+  if (pks > 1 && (workspace == nullptr || workspace_elems < (int64_t)pks * M * N)) pks = 1;
+  if (M >= RB_GEMM_PAIR_MIN_M || pks > 1) {
     // two-SM tiles: each CTA of a pair loads 128 rows of A and BN/2 of B.  A
     // 128-wide tile re-reads A twice as often and runs about 1.45x longer per
     // output column than a 256-wide one (L2-bound: K = 14336, N = 512 on a
@@ -1890,7 +1993,12 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
     const int64_t t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128);
     const int64_t cost256 = 4 * ((t256 + pairs_avail - 1) / pairs_avail);  // in quarter-units of a 128-wide tile
     const int64_t cost128 = 3 * ((t128 + pairs_avail - 1) / pairs_avail);
-    const bool narrow = cost128 < cost256;
+    // too few tiles for half the pairs: 256-wide tiles split along K instead
+    if (pks > 1) {
+      ep.ksplits = pks;
+      ep.partials = workspace;
+    }
+    const bool narrow = pks == 1 && cost128 < cost256;
     const int bn = narrow ? 128 : 256;
     CUtensorMap tpA, tpB;
     rc = make_tmap(&tpA, A, K, M, lda, pair::BK, 128);
@@ -1906,7 +2014,7 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
                                   pair::Cfg<128>::SMEM_BYTES);
     });
     if (pe != cudaSuccess) return check_cuda(pe, "cudaFuncSetAttribute(w8a8_gemm_tc_pair_kernel)");
-    const int64_t ptiles = narrow ? t128 : t256;
+    const int64_t ptiles = (narrow ? t128 : t256) * pks;
     const int pairs = (int)std::min<int64_t>(ptiles, pairs_avail);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
@@ -1923,8 +2031,10 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
     if (narrow)
       return check_cuda(cudaLaunchKernelEx(&cfg, pair::w8a8_gemm_tc_pair_kernel<128>, tpA, tpB, ep),
                         "w8a8_gemm_tc_pair_kernel<128> launch");
-    return check_cuda(cudaLaunchKernelEx(&cfg, pair::w8a8_gemm_tc_pair_kernel<256>, tpA, tpB, ep),
-                      "w8a8_gemm_tc_pair_kernel<256> launch");
+    rc = check_cuda(cudaLaunchKernelEx(&cfg, pair::w8a8_gemm_tc_pair_kernel<256>, tpA, tpB, ep),
+                    "w8a8_gemm_tc_pair_kernel<256> launch");
+    if (rc || pks == 1) return rc;
+    return launch_splitk_finalize(ep, st);
   }
   // one-SM tiles, split along K when the (m, n) tiles alone cannot fill the GPU
   int ks = choose_ksplits(M, N, K);
@@ -1951,10 +2061,7 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
   w8a8_gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tmA, tmB, ep);
   rc = check_cuda(cudaGetLastError(), "w8a8_gemm_tc_kernel launch");
   if (rc || ep.ksplits == 1) return rc;
-  const int64_t total = M * N;
-  const int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)sm_count() * 8);
-  splitk_finalize_kernel<<<(unsigned)blocks, 256, 0, st>>>(ep);
-  return check_cuda(cudaGetLastError(), "splitk_finalize_kernel launch");
+  return launch_splitk_finalize(ep, st);
 }
 
 extern "C" int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int64_t M, int64_t N,

@@ -56,8 +56,9 @@ def test_gemm_golden(cuda_device):
                                    # M <= 16: one 16-byte K chunk, K over one round of
                                    # 128 chunks per CTA, column counts off the 16-column groups
                                    (3, 16, 48), (16, 16400, 40), (9, 2064, 17), (2, 14336, 1),
-                                   # CTA-pair path (M >= 4096) with ragged M, N and K blocks
-                                   (4099, 1040, 300), (6000, 592, 48), (8191, 14336, 512)])
+                                   # CTA-pair path (M >= 4096) with ragged M, N and K blocks; up to
+                                   # half the pairs' worth of tiles it splits K (2 or 4 ways here)
+                                   (4099, 1040, 300), (6000, 592, 48), (8191, 14336, 512), (4500, 2080, 130)])
 def test_gemm_random_shapes(cuda_device, M, K, N):
     import torch
     from oracle import oracle as O
