@@ -948,7 +948,7 @@ def gemm_sweep(args):
     def flush():
         scrub.fill_(1)
 
-    for M in (1, 16, 64, 128, 256, 1024, 4096, 8192, 32768, 131072):
+    for M in (1, 16, 64, 128, 256, 512, 1024, 2048, 4096, 8192, 32768, 131072):
         a = torch.randint(-127, 128, (M, H), dtype=torch.int8, device=dev, generator=gen)
         sa = torch.rand(M, device=dev, generator=gen) * 9e-3 + 1e-3
         out = torch.empty((M, D_OUT), dtype=torch.bfloat16, device=dev)
