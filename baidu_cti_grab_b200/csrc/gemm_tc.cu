@@ -1302,6 +1302,24 @@ __global__ void __launch_bounds__(kGvThreads * gv_groups(MT), gv_groups(MT) > 1 
   const int64_t per_cta = (chunks + kGvSplit - 1) / kGvSplit;
   const int64_t k0 = (int64_t)rank * per_cta;
   const int64_t k_end = min(chunks, k0 + per_cta);
+  // Programmatic dependent launch: the next kernel on the stream may start now
+  // (a kernel launched that way waits for this grid to complete before it
+  // reads what this grid writes).  While the previous kernel finishes, this
+  // CTA requests its weight slice into L2, then waits until that kernel's
+  // writes are visible before it reads anything.  A prefetch has no
+  // architectural effect: a weight written by the previous kernel is still
+  // read fresh from L2 after the wait.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (k_end > k0) {
+    const int64_t seg = (k_end - k0) * 16;  // bytes of one weight row in this CTA's K range
+    const int lines = (int)((seg + 127) / 128);
+    for (int i = threadIdx.x; i < kGvCols * lines; i += kThreads) {
+      const int64_t n = n0 + i / lines;
+      const int64_t off = min((int64_t)(i % lines) * 128, seg - 1);
+      if (n < ep.N) asm volatile("prefetch.global.L2 [%0];" ::"l"(B + n * ldb + k0 * 16 + off));
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // the leader's epilogue operands, requested now so that their latency
   // overlaps the loads and products instead of following the last barrier
   constexpr int kPer = (MT * kGvCols + kThreads - 1) / kThreads;
@@ -1590,9 +1608,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
+  // Programmatic dependent launch (as in w8a8_gemv_kernel): the next kernel
+  // may start; while the previous kernel finishes, this CTA requests its
+  // weight boxes into L2 (a prefetch has no architectural effect) and sets up
+  // its barriers and TMEM; every read of data follows griddepcontrol.wait.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (warp == 0 && lane == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    for (int kb = kb0; kb < kb1; ++kb)
+      asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                       reinterpret_cast<uint64_t>(&tmW)),
+                   "r"(kb * BK), "r"((int)n_tile0)
+                   : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -1604,6 +1632,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0 && has_k) {
@@ -1929,13 +1958,17 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
     cfg.blockDim = dim3(kGvThreads * (M > 8 ? gv_groups(16) : 1));
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = kGvSplit;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // may start before the previous kernel on the stream completes (the
+    // kernel's griddepcontrol.wait orders every read after that kernel)
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t le;
     if (M <= 1) le = cudaLaunchKernelEx(&cfg, w8a8_gemv_kernel<1>, A, lda, B, ldb, ep);
     else if (M <= 2) le = cudaLaunchKernelEx(&cfg, w8a8_gemv_kernel<2>, A, lda, B, ldb, ep);
@@ -1969,13 +2002,15 @@ extern "C" int rb_w8a8_gemm_ws(const int8_t* A, int64_t lda, const int8_t* B, in
     cfg.blockDim = dim3(swp::NUM_THREADS);
     cfg.dynamicSmemBytes = swp::SMEM_BYTES;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = swp::kSplit;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see w8a8_gemv_kernel
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return check_cuda(cudaLaunchKernelEx(&cfg, swp::w8a8_gemm_swap_kernel, tmW, tmAct, ep, mp),
                       "w8a8_gemm_swap_kernel launch");
   }
