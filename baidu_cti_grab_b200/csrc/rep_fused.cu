@@ -99,10 +99,22 @@ __device__ __forceinline__ void round_half_away2(F2 v, int& q0, int& q1) {
   q1 = __float2int_rz(r.y);
 }
 
-__device__ __forceinline__ uint32_t pack_i8x4_prmt(int a, int b, int c, int d) {
-  const uint32_t ab = __byte_perm((uint32_t)a, (uint32_t)b, 0x0040);
-  const uint32_t cd = __byte_perm((uint32_t)c, (uint32_t)d, 0x0040);
-  return __byte_perm(ab, cd, 0x5410);
+// four int32 values (each in [-128, 127]) as bytes a, b, c, d of one word:
+// cvt.pack.sat puts its second operand in the low byte, its first in the next
+// and the low 16 bits of its third above them
+__device__ __forceinline__ uint32_t pack_i8x4_sat(int a, int b, int c, int d) {
+  uint32_t hi, r;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(d), "r"(c), "r"(0u));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(b), "r"(a), "r"(hi));
+  return r;
+}
+
+// running absmax of packed bf16 pairs: each half keeps max(|acc|, |w|) (the
+// sign of the result is the xor of the operands' signs and is discarded)
+__device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t acc, uint32_t w) {
+  uint32_t r;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(w));
+  return r;
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -630,6 +642,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
     // ---- y = fma(rstd * (x - mean), gamma, beta) rounded to T, in place; absmax
     // (a rolled loop: the smaller code measured 2 % faster than four copies)
     float amax = 0.0f;
+    uint32_t amax2 = 0u;  // bf16 rows: running absmax of the rounded pairs
 #pragma unroll 1
     for (int j = 0; j < kSlotsPerWarp; ++j) {
       if (j >= nsl) break;
@@ -642,10 +655,9 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
         for (int i = 0; i < 8; ++i) {
           const F2 d = f2(sub_lo(w[i], mean), sub_hi(w[i], mean));
           const float2 v = un(fma2(mul2(rstd2, d), aff.gamma(i, bf_affine), aff.beta(i, bf_affine)));
-          // rounding to bf16 is monotonic and symmetric, so the absmax of the
-          // rounded row is the rounded absmax of the fp32 row
-          amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
           w[i] = pack_bf16x2(v.x, v.y);
+          // the quantiser's absmax is over the rounded row
+          amax2 = absmax_bf16x2(amax2, w[i]);
         }
         st_words(s_words + s * 256, lane, w);
         if (!kPlain && p.ln != nullptr) st_words(reinterpret_cast<T*>(p.ln) + item * (int64_t)(S * kDim) + s * kDim, lane, w);
@@ -665,7 +677,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
       }
     }
     if (!kPlain && p.act_mode == RB_ACT_NONE) return;
-    if constexpr (kBf16) amax = round_bf16(amax);
+    if constexpr (kBf16) amax = fmaxf(fabsf(bf16_lo(amax2)), fabsf(bf16_hi(amax2)));
     amax = warp_max(amax);
     if (lane == 0) s_wmax[warp] = amax;
     __syncthreads();
@@ -709,10 +721,10 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 3) rep_fused_kernel(
         round_half_away2(v, q[2 * i], q[2 * i + 1]);
       }
       int8_t* dst = q_lane + s * kDim;
-      *reinterpret_cast<uint2*>(dst) = make_uint2(pack_i8x4_prmt(q[0], q[1], q[2], q[3]),
-                                                  pack_i8x4_prmt(q[4], q[5], q[6], q[7]));
-      *reinterpret_cast<uint2*>(dst + 256) = make_uint2(pack_i8x4_prmt(q[8], q[9], q[10], q[11]),
-                                                        pack_i8x4_prmt(q[12], q[13], q[14], q[15]));
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack_i8x4_sat(q[0], q[1], q[2], q[3]),
+                                                  pack_i8x4_sat(q[4], q[5], q[6], q[7]));
+      *reinterpret_cast<uint2*>(dst + 256) = make_uint2(pack_i8x4_sat(q[8], q[9], q[10], q[11]),
+                                                        pack_i8x4_sat(q[12], q[13], q[14], q[15]));
     }
   }
 }
