@@ -7,23 +7,23 @@
 // count, models.py:160), runs two bmm's with the stacked expert weights and
 // scatters the score-weighted rows back with index_add_.  Here:
 //
-//   route_count_kernel     per chunk of 1024 entries, how many go to each expert
+//   route_count_kernel     per chunk of 256 entries, how many go to each expert
 //   route_scatter_kernel   stable counting sort (the order of
 //                          torch.argsort(stable=True)): expert offsets, the
 //                          sorted entry list, and the packed rows
 //                          packed[p] = x[entry / k] of each expert's segment
-//   moe_gemm_kernel<1>     per expert segment, hidden = relu(x W1^T + b1)
-//   moe_gemm_kernel<2>     per expert segment, y[entry] = (h W2^T + b2) * score
+//   moe_gemm_pair_kernel<1>  per expert segment, hidden = relu(x W1^T + b1)
+//   moe_gemm_pair_kernel<2>  per expert segment, y[entry] = (h W2^T + b2) * score
 //   combine_kernel         out[t] = y[t*k] + y[t*k+1] + ... in slot order
 //
 // The grouped GEMMs read the expert offsets on the device: a persistent CTA
-// walks tiles (expert, 128-row block, 256-column block) until the last
+// pair walks tiles (expert, 256-row block, 256-column block) until the last
 // expert's rows are covered, so nothing is read back by the host and no row
-// of padding is multiplied.  They are the one-SM tcgen05 pipeline of
-// gemm_tc.cu (TMA -> 4-stage ring -> kind::f16 MMA into two 128x256 fp32
-// TMEM accumulators -> epilogue warps), with a per-tile B row offset of
-// expert * N.  Rows of a 128-row block past its expert's segment are computed
-// and discarded.
+// of padding is multiplied.  They follow the CTA-pair tcgen05 pipeline of
+// gemm_tc.cu (TMA -> 6-stage ring per CTA -> kind::f16 MMA of the pair into
+// two 256x256 fp32 TMEM accumulators -> epilogue warps), with a per-tile B row
+// offset of expert * N.  Rows of a 256-row block past its expert's segment are
+// computed and discarded.
 //
 // Rounding follows the reference's bf16/fp16 torch ops step by step: the bmm
 // result rounded to the model dtype, + bias (rounded), relu; the second bmm
@@ -40,7 +40,7 @@ namespace moe {
 
 constexpr int kMaxExperts = 64;
 constexpr int kRouteThreads = 256;
-constexpr int kRouteChunk = 1024;  // entries per CTA, in rounds of kRouteThreads
+constexpr int kRouteChunk = 256;  // entries per CTA (one round of kRouteThreads): enough CTAs to fill the SMs
 constexpr int kMoeBadExpert = 301;  // watchdog code: an expert id outside [0, E)
 
 template <typename IdxT>
@@ -207,38 +207,38 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, c
 
 // ------------------------------------------------------------ grouped GEMM
 using tc::BK;
-using tc::BM;
-using tc::BN;
-using tc::STAGES;
-using tc::A_BYTES;
-using tc::B_BYTES;
-using tc::STAGE_BYTES;
-using tc::SMEM_BYTES;
-using tc::NUM_THREADS;
-using tc::EPI_THREADS;
-using tc::TMEM_COLS;
 
-constexpr int MMA_KB = 32;  // K bytes per tcgen05.mma kind::f16 (16 elements)
+constexpr int MMA_KB = 32;      // K bytes per tcgen05.mma kind::f16 (16 elements)
+constexpr int kPairRows = 256;  // rows of a tile (128 per CTA of the pair)
+constexpr int kTileCols = 256;  // columns of a tile
+// a TMA warp, an MMA warp and eight epilogue warps (two per TMEM lane quarter,
+// one per half of the tile's columns)
+constexpr int kMoeEpiWarps = 8;
+constexpr int kMoeThreads = 64 + 32 * kMoeEpiWarps;
+using PairCfg = tc::pair::Cfg<256>;  // 6-stage ring of 16 KB of A + 16 KB of B per CTA, 512 TMEM columns
 
+// instruction descriptor: D = F32, A/B = BF16 or F16, both K-major, M = 256 (the pair), N = 256
 template <typename T>
-struct F16Kind;
+struct F16KindPair;
 template <>
-struct F16Kind<__nv_bfloat16> {  // D = F32, A/B = BF16, K-major, M = 128, N = 256
-  static constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                                    ((uint32_t)(BM >> 4) << 24);
+struct F16KindPair<__nv_bfloat16> {
+  static constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileCols >> 3) << 17) |
+                                    ((uint32_t)(kPairRows >> 4) << 24);
 };
 template <>
-struct F16Kind<__half> {  // D = F32, A/B = F16
-  static constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+struct F16KindPair<__half> {
+  static constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(kTileCols >> 3) << 17) | ((uint32_t)(kPairRows >> 4) << 24);
 };
 
 template <typename T>
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(F16Kind<T>::idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(F16KindPair<T>::idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
+      "r"(0u), "r"(0u), "r"(0u));
 }
 
 struct MoeGemmParams {
@@ -258,37 +258,151 @@ __device__ __forceinline__ float round_to(float v) {
   return (float)T(v);
 }
 
+// Epilogue of one finished 128-row x 256-column accumulator (this CTA's rows
+// m0 .. m0+127 of expert e, columns n0 ..): a warp with TMEM lane quarter
+// `quarter` reads lanes 32*quarter.. of the 32-column chunks c_begin ..
+// c_end-1 of the accumulator at TMEM column t_acc, rounds as the reference's
+// torch ops do and stores the live rows (below m_end).
 template <int EPI, typename T>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
-    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ MoeGemmParams p) {
+__device__ __forceinline__ void moe_epilogue_tile(const MoeGemmParams& p, int e, int m0, int m_end, int n0,
+                                                  int quarter, int lane, uint32_t t_acc, int c_begin, int c_end) {
+  const T* bias = reinterpret_cast<const T*>(p.bias);
+  const int row = m0 + quarter * 32 + lane;
+  const bool live = row < m_end;
+  int64_t orow = row;
+  float w = 0.0f;
+  if (EPI == 2 && live) {
+    const int32_t entry = p.sorted_entry[row];
+    orow = entry;
+    w = (float)reinterpret_cast<const T*>(p.score)[entry];
+  }
+#pragma unroll 1
+  for (int c = c_begin; c < c_end; ++c) {
+    const int col0 = n0 + c * 32;
+    if (col0 >= p.N) break;  // warp-uniform
+    uint32_t r[32];
+    tc::tmem_ld32(t_acc + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32), r);
+    if (!live) continue;
+    // the chunk's 32 bias values: four 16-byte loads when aligned
+    T bv[32];
+    if (bias != nullptr) {
+      const T* bp = bias + (int64_t)e * p.N + col0;
+      if ((reinterpret_cast<uintptr_t>(bp) & 15) == 0 && col0 + 32 <= p.N) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(bv + 8 * q) = reinterpret_cast<const uint4*>(bp)[q];
+      } else {
+#pragma unroll
+        for (int q = 0; q < 32; ++q) bv[q] = col0 + q < p.N ? bp[q] : T(0.0f);
+      }
+    }
+    uint32_t packed[16];
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      if (bias != nullptr) {
+        // bf16 with bias, pairs of columns: the bmm result rounded (one
+        // cvt for both), widened, + bias as the bf16 operand of a mixed
+        // fp32 add, then (1) relu before the rounding -- exact here: a sum
+        // of two bf16 values is 0, -0 or at least 2^-133 in magnitude, so
+        // it is negative exactly when its rounding is -- or (2) rounded,
+        // widened, times the score and rounded; one cvt packs each pair
+        const uint32_t* bw = reinterpret_cast<const uint32_t*>(bv);
+        const F2 w2 = f2(w, w);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const uint32_t p1 = pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+          float lo = add_lo(bf16_lo(p1), bw[j]), hi = add_hi(bf16_hi(p1), bw[j]);
+          if (EPI == 1) {
+            lo = lo < 0.0f ? 0.0f : lo;
+            hi = hi < 0.0f ? 0.0f : hi;
+            packed[j] = pack_bf16x2(lo, hi);
+          } else {
+            const uint32_t p2 = pack_bf16x2(lo, hi);
+            const float2 v = un(mul2v(f2(bf16_lo(p2), bf16_hi(p2)), w2));
+            packed[j] = pack_bf16x2(v.x, v.y);
+          }
+        }
+        T* dst = reinterpret_cast<T*>(p.out) + orow * p.ldo + col0;
+        stg_v8(dst, packed);
+        stg_v8(dst + 16, packed + 8);
+        continue;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float v2[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float v = round_to<T>(__uint_as_float(r[2 * j + h]));
+        if (bias != nullptr) v = round_to<T>(__fadd_rn(v, (float)bv[2 * j + h]));
+        if (EPI == 1) {
+          v = v < 0.0f ? 0.0f : v;
+        } else {
+          v = round_to<T>(__fmul_rn(v, w));
+        }
+        v2[h] = v;
+      }
+      T lo = T(v2[0]), hi = T(v2[1]);
+      packed[j] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+    }
+    T* dst = reinterpret_cast<T*>(p.out) + orow * p.ldo + col0;
+    stg_v8(dst, packed);
+    stg_v8(dst + 16, packed + 8);
+  }
+}
+
+// The grouped GEMM on CTA pairs: a cluster of two CTAs computes each 256 x 256
+// tile (expert, 256-row block, 256-column block) with
+// tcgen05.mma.cta_group::2 issued by the leader; each CTA TMA-loads its own 128
+// rows of A and 128 rows of B per stage (no multicast) and signals the leader's
+// full barrier, and the leader's commits arrive on both CTAs' barriers.  Per SM
+// a stage carries 16 KB of A and 16 KB of B for the MMA work that costs a
+// one-SM 128 x 256 tile 16 KB of A and 32 KB of B.  A persistent pair walks the
+// tiles of all experts, reading the segment offsets on the device; rows of a
+// block past its expert's segment are computed and discarded.  Each CTA's
+// eight epilogue warps round and store its 128 rows, two warps per TMEM lane
+// quarter (one per half of the columns): at d_model 512 a tile's main loop is
+// only 8 (FC1) or 16 (FC2) ring stages, and four epilogue warps fell behind
+// it.  The epilogue warps of both CTAs release an accumulator on the leader's
+// barrier.
+template <int EPI, typename T>
+__global__ void __launch_bounds__(kMoeThreads, 1)
+    moe_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ MoeGemmParams p) {
+  namespace pr = tc::pair;
+  constexpr int kStages = PairCfg::STAGES;
+  constexpr int kStageBytes = PairCfg::STAGE_BYTES;
+  constexpr int kABytes = pr::A_BYTES;
+  constexpr int kBBytes = PairCfg::B_BYTES;
+  constexpr int kTmemCols = PairCfg::TMEM_COLS;
+  constexpr int kElt = (int)sizeof(T);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* tfull = bars + 2 * STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* done = tempty + 2;
+  uint8_t* sB = smem + kStages * kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* full = bars;                 // [kStages]  leader: TMA bytes of both CTAs -> MMA
+  uint64_t* empty = bars + kStages;      // [kStages]  both: MMA done with the slot -> TMA
+  uint64_t* tfull = bars + 2 * kStages;  // [2]        both: accumulator ready -> epilogue
+  uint64_t* tempty = tfull + 2;          // [2]        leader: both epilogues done -> MMA
+  uint64_t* done = tempty + 2;           // [1]        leader: all MMAs complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   __shared__ int s_off[kMaxExperts + 1];
-  __shared__ int s_mt[kMaxExperts + 1];  // prefix of 128-row blocks per expert
+  __shared__ int s_mt[kMaxExperts + 1];  // prefix of 256-row blocks per expert
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = pr::cluster_rank();
+  const bool leader = rank == 0;
   const int E = p.E;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&tfull[b]), 1);
-      mbar_init(smem_u32(&tempty[b]), EPI_THREADS);
+      mbar_init(smem_u32(&tempty[b]), 2 * kMoeEpiWarps);  // one arrival per epilogue warp of both CTAs
     }
     mbar_init(smem_u32(done), 1);
     *abort_flag = 0;
@@ -297,7 +411,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int a = p.offsets[e], b = p.offsets[e + 1];
       s_off[e] = a;
       s_mt[e] = mt;
-      mt += (b - a + BM - 1) / BM;
+      mt += (b - a + kPairRows - 1) / kPairRows;
     }
     s_off[E] = p.offsets[E];
     s_mt[E] = mt;
@@ -309,188 +423,128 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS)
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   tc::tc_fence_before();
   __syncthreads();
+  pr::cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int n_tiles = (p.N + BN - 1) / BN;
+  const int n_tiles = (p.N + kTileCols - 1) / kTileCols;
   const int64_t num_tiles = (int64_t)s_mt[E] * n_tiles;
-  const int kblocks = (int)(((int64_t)p.K * (int64_t)sizeof(T) + BK - 1) / BK);
-  constexpr int kElt = (int)sizeof(T);
-  // tile -> (expert, first row, last row + 1, first column); n is the fastest
-  // index so CTAs running side by side share their A rows in L2
+  const int kblocks = (int)(((int64_t)p.K * kElt + BK - 1) / BK);
+  const int64_t pair_id = blockIdx.x >> 1;
+  const int64_t num_pairs = gridDim.x >> 1;
+  // tile -> (expert, first row of the tile, end of the expert's rows, first
+  // column); n is the fastest index so pairs running side by side share their
+  // A rows in L2
   auto locate = [&](int64_t tile, int& e, int& m0, int& m_end, int& n0) {
     const int mg = (int)(tile / n_tiles);
-    n0 = (int)(tile % n_tiles) * BN;
+    n0 = (int)(tile % n_tiles) * kTileCols;
     e = 0;
     while (e + 1 < E && s_mt[e + 1] <= mg) ++e;
-    m0 = s_off[e] + (mg - s_mt[e]) * BM;
+    m0 = s_off[e] + (mg - s_mt[e]) * kPairRows;
     m_end = s_off[e + 1];
   };
 
   if (warp == 0) {
     if (lane == 0) {
+      // ---------------------------------------------------------- producer
       const uint64_t pol_a = tc::policy_evict_first(), pol_b = tc::policy_evict_last();
       int stage = 0;
       uint32_t phase = 0, issued = 0, issued_phase = 0;
       bool ok = true;
-      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int64_t tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
         int e, m0, m_end, n0;
         locate(tile, e, m0, m_end, n0);
+        const int arow = m0 + (int)rank * 128;
+        const int brow = e * p.N + n0 + (int)rank * 128;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait_bounded(smem_u32(&empty[stage]), phase ^ 1, kWaitTimeoutProducer, abort_flag)) {
             ok = false;
             break;
           }
-          const uint32_t fb = smem_u32(&full[stage]);
-          mbar_arrive_expect_tx(fb, STAGE_BYTES);
-          tc::tma_load_2d(smem_u32(sA + stage * A_BYTES), &tmA, kb * (BK / kElt), m0, fb, pol_a);
-          tc::tma_load_2d(smem_u32(sB + stage * B_BYTES), &tmB, kb * (BK / kElt), e * p.N + n0, fb, pol_b);
+          const uint32_t fb_local = smem_u32(&full[stage]);
+          if (leader) mbar_arrive_expect_tx(fb_local, 2 * kStageBytes);
+          const uint32_t fb = pr::map_rank(fb_local, 0);
+          pr::tma_load_2d_pair(smem_u32(sA + stage * kABytes), &tmA, kb * (BK / kElt), arow, fb, pol_a);
+          pr::tma_load_2d_pair(smem_u32(sB + stage * kBBytes), &tmB, kb * (BK / kElt), brow, fb, pol_b);
           issued |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
-          if (++stage == STAGES) {
+          if (++stage == kStages) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      for (int s = 0; s < STAGES; ++s)
-        if (issued & (1u << s))
-          mbar_wait_bounded(smem_u32(&full[s]), (issued_phase >> s) & 1u, kWaitTimeoutProducer, nullptr);
+      if (leader) {
+        // the leader's full barriers count both CTAs' bytes: drain them before exit
+        for (int s = 0; s < kStages; ++s)
+          if (issued & (1u << s))
+            mbar_wait_bounded(smem_u32(&full[s]), (issued_phase >> s) & 1u, kWaitTimeoutProducer, nullptr);
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && leader) {
+      // --------------------------------------------------------------- MMA
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int64_t tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
         if (!mbar_wait_bounded(smem_u32(&tempty[acc]), acc_phase ^ 1, kWaitTimeoutMma, abort_flag)) break;
         tc::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kTileCols);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait_bounded(smem_u32(&full[stage]), phase, kWaitTimeoutMma, abort_flag)) {
             ok = false;
             break;
           }
           tc::tc_fence_after();
-          const uint64_t adesc = tc::sw128_desc(smem_u32(sA + stage * A_BYTES));
-          const uint64_t bdesc = tc::sw128_desc(smem_u32(sB + stage * B_BYTES));
+          const uint64_t adesc = tc::sw128_desc(smem_u32(sA + stage * kABytes));
+          const uint64_t bdesc = tc::sw128_desc(smem_u32(sB + stage * kBBytes));
 #pragma unroll
           for (int s = 0; s < BK / MMA_KB; ++s)
-            umma_f16<T>(d_tmem, adesc + (uint64_t)(s * MMA_KB / 16), bdesc + (uint64_t)(s * MMA_KB / 16),
-                        (kb > 0 || s > 0) ? 1u : 0u);
-          tc::umma_commit(smem_u32(&empty[stage]));
-          if (++stage == STAGES) {
+            umma_f16_pair<T>(d_tmem, adesc + (uint64_t)(s * MMA_KB / 16), bdesc + (uint64_t)(s * MMA_KB / 16),
+                             (kb > 0 || s > 0) ? 1u : 0u);
+          pr::umma_commit_both(smem_u32(&empty[stage]));
+          if (++stage == kStages) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        tc::umma_commit(smem_u32(&tfull[acc]));
+        pr::umma_commit_both(smem_u32(&tfull[acc]));
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
-      tc::umma_commit(smem_u32(done));
+      asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       smem_u32(done))
+                   : "memory");
       mbar_wait_bounded(smem_u32(done), 0, kWaitTimeoutMma, nullptr);
     }
   } else {
-    const int quarter = warp & 3;
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // the TMEM lanes this warp can read
+    constexpr int kChunks = kTileCols / 32 / (kMoeEpiWarps / 4);  // 32-column chunks per epilogue warp
+    const int c_begin = ((warp - 2) >> 2) * kChunks;
+    const uint32_t tempty_leader0 = pr::map_rank(smem_u32(&tempty[0]), 0);
+    const uint32_t tempty_leader1 = pr::map_rank(smem_u32(&tempty[1]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    const T* bias = reinterpret_cast<const T*>(p.bias);
-    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int64_t tile = pair_id; tile < num_tiles; tile += num_pairs) {
       int e, m0, m_end, n0;
       locate(tile, e, m0, m_end, n0);
       if (!mbar_wait_bounded(smem_u32(&tfull[acc]), acc_phase, kWaitTimeoutEpilogue, abort_flag)) break;
       tc::tc_fence_after();
-      const int row = m0 + quarter * 32 + lane;
-      const bool live = row < m_end;
-      int64_t orow = row;
-      float w = 0.0f;
-      if (EPI == 2 && live) {
-        const int32_t entry = p.sorted_entry[row];
-        orow = entry;
-        w = (float)reinterpret_cast<const T*>(p.score)[entry];
-      }
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int col0 = n0 + c * 32;
-        if (col0 >= p.N) break;  // warp-uniform
-        uint32_t r[32];
-        tc::tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-        if (!live) continue;
-        // the chunk's 32 bias values: four 16-byte loads when aligned
-        T bv[32];
-        if (bias != nullptr) {
-          const T* bp = bias + (int64_t)e * p.N + col0;
-          if ((reinterpret_cast<uintptr_t>(bp) & 15) == 0 && col0 + 32 <= p.N) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(bv + 8 * q) = reinterpret_cast<const uint4*>(bp)[q];
-          } else {
-#pragma unroll
-            for (int q = 0; q < 32; ++q) bv[q] = col0 + q < p.N ? bp[q] : T(0.0f);
-          }
-        }
-        uint32_t packed[16];
-        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-          if (bias != nullptr) {
-            // bf16 with bias, pairs of columns: the bmm result rounded (one
-            // cvt for both), widened, + bias as the bf16 operand of a mixed
-            // fp32 add, then (1) relu before the rounding -- exact here: a sum
-            // of two bf16 values is 0, -0 or at least 2^-133 in magnitude, so
-            // it is negative exactly when its rounding is -- or (2) rounded,
-            // widened, times the score and rounded; one cvt packs each pair
-            const uint32_t* bw = reinterpret_cast<const uint32_t*>(bv);
-            const F2 w2 = f2(w, w);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const uint32_t p1 = pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-              float lo = add_lo(bf16_lo(p1), bw[j]), hi = add_hi(bf16_hi(p1), bw[j]);
-              if (EPI == 1) {
-                lo = lo < 0.0f ? 0.0f : lo;
-                hi = hi < 0.0f ? 0.0f : hi;
-                packed[j] = pack_bf16x2(lo, hi);
-              } else {
-                const uint32_t p2 = pack_bf16x2(lo, hi);
-                const float2 v = un(mul2v(f2(bf16_lo(p2), bf16_hi(p2)), w2));
-                packed[j] = pack_bf16x2(v.x, v.y);
-              }
-            }
-            T* dst = reinterpret_cast<T*>(p.out) + orow * p.ldo + col0;
-            stg_v8(dst, packed);
-            stg_v8(dst + 16, packed + 8);
-            continue;
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float v2[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float v = round_to<T>(__uint_as_float(r[2 * j + h]));
-            if (bias != nullptr) v = round_to<T>(__fadd_rn(v, (float)bv[2 * j + h]));
-            if (EPI == 1) {
-              v = v < 0.0f ? 0.0f : v;
-            } else {
-              v = round_to<T>(__fmul_rn(v, w));
-            }
-            v2[h] = v;
-          }
-          T lo = T(v2[0]), hi = T(v2[1]);
-          packed[j] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
-        }
-        T* dst = reinterpret_cast<T*>(p.out) + orow * p.ldo + col0;
-        stg_v8(dst, packed);
-        stg_v8(dst + 16, packed + 8);
-      }
+      moe_epilogue_tile<EPI, T>(p, e, m0 + (int)rank * 128, m_end, n0, quarter, lane,
+                                tmem_base + (uint32_t)(acc * kTileCols), c_begin, c_begin + kChunks);
       tc::tc_fence_before();
-      mbar_arrive(smem_u32(&tempty[acc]));
+      __syncwarp();
+      if (lane == 0) pr::mbar_arrive_remote(acc ? tempty_leader1 : tempty_leader0);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
@@ -498,13 +552,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc::tc_fence_before();
   __syncthreads();
+  pr::cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers
   if (warp == 1) {
     tc::tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
                  : "memory");
   }
 }
-
 static std::once_flag g_moe_attr_once[64];
 
 struct Workspace {
@@ -594,25 +648,25 @@ extern "C" int rb_smoe_experts(const void* x, int x_dtype, int64_t ldx, int64_t 
   if (rc) return rc;
 
   const CUtensorMapDataType dt = x_dtype == RB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  // A in 128-row boxes, B in 128-row boxes: each CTA of a pair loads its half of a 256 x 256 tile
   CUtensorMap tA1, tB1, tA2, tB2;
-  if ((rc = tc::make_tmap(&tA1, ws.rows, D, R, (int64_t)D * elt, tc::BK / elt, tc::BM, dt))) return rc;
-  if ((rc = tc::make_tmap(&tB1, w1, D, (int64_t)E * F, (int64_t)D * elt, tc::BK / elt, tc::BN, dt))) return rc;
-  if ((rc = tc::make_tmap(&tA2, ws.hidden, F, R, (int64_t)F * elt, tc::BK / elt, tc::BM, dt))) return rc;
-  if ((rc = tc::make_tmap(&tB2, w2, F, (int64_t)E * D, (int64_t)F * elt, tc::BK / elt, tc::BN, dt))) return rc;
+  if ((rc = tc::make_tmap(&tA1, ws.rows, D, R, (int64_t)D * elt, tc::BK / elt, 128, dt))) return rc;
+  if ((rc = tc::make_tmap(&tB1, w1, D, (int64_t)E * F, (int64_t)D * elt, tc::BK / elt, 128, dt))) return rc;
+  if ((rc = tc::make_tmap(&tA2, ws.hidden, F, R, (int64_t)F * elt, tc::BK / elt, 128, dt))) return rc;
+  if ((rc = tc::make_tmap(&tB2, w2, F, (int64_t)E * D, (int64_t)F * elt, tc::BK / elt, 128, dt))) return rc;
   int dev = 0;
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(g_moe_attr_once[dev & 63], [&] {
-    const void* fns[4] = {(const void*)moe_gemm_kernel<1, __nv_bfloat16>, (const void*)moe_gemm_kernel<2, __nv_bfloat16>,
-                          (const void*)moe_gemm_kernel<1, __half>, (const void*)moe_gemm_kernel<2, __half>};
+    const void* fns[4] = {(const void*)moe_gemm_pair_kernel<1, __nv_bfloat16>,
+                          (const void*)moe_gemm_pair_kernel<2, __nv_bfloat16>,
+                          (const void*)moe_gemm_pair_kernel<1, __half>, (const void*)moe_gemm_pair_kernel<2, __half>};
     for (const void* f : fns)
       if (attr_err == cudaSuccess)
-        attr_err = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);
+        attr_err = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::SMEM_BYTES);
   });
-  if (attr_err != cudaSuccess) return check_cuda(attr_err, "cudaFuncSetAttribute(moe_gemm_kernel)");
+  if (attr_err != cudaSuccess) return check_cuda(attr_err, "cudaFuncSetAttribute(moe_gemm_pair_kernel)");
 
-  // upper bound of the 128-row blocks over all experts: ceil(R / 128) + E
-  const int64_t mblocks = (R + tc::BM - 1) / tc::BM + E;
   MoeGemmParams p1{};
   p1.offsets = ws.offsets;
   p1.bias = b1;
@@ -629,17 +683,33 @@ extern "C" int rb_smoe_experts(const void* x, int x_dtype, int64_t ldx, int64_t 
   p2.ldo = D;
   p2.N = D;
   p2.K = F;
-  const int grid1 = (int)std::min<int64_t>(mblocks * ((F + tc::BN - 1) / tc::BN), sm_count());
-  const int grid2 = (int)std::min<int64_t>(mblocks * ((D + tc::BN - 1) / tc::BN), sm_count());
+  // upper bound of the 256-row blocks over all experts: ceil(R / 256) + E
+  const int64_t pblocks = (R + kPairRows - 1) / kPairRows + E;
+  const int pairs_avail = sm_count() / 2;
+  const int pairs1 = (int)std::min<int64_t>(pblocks * ((F + kTileCols - 1) / kTileCols), pairs_avail);
+  const int pairs2 = (int)std::min<int64_t>(pblocks * ((D + kTileCols - 1) / kTileCols), pairs_avail);
   const unsigned cgrid = (unsigned)((T + 7) / 8);
-  if (x_dtype == RB_BF16) {
-    moe_gemm_kernel<1, __nv_bfloat16><<<grid1, tc::NUM_THREADS, tc::SMEM_BYTES, st>>>(tA1, tB1, p1);
-    moe_gemm_kernel<2, __nv_bfloat16><<<grid2, tc::NUM_THREADS, tc::SMEM_BYTES, st>>>(tA2, tB2, p2);
-  } else {
-    moe_gemm_kernel<1, __half><<<grid1, tc::NUM_THREADS, tc::SMEM_BYTES, st>>>(tA1, tB1, p1);
-    moe_gemm_kernel<2, __half><<<grid2, tc::NUM_THREADS, tc::SMEM_BYTES, st>>>(tA2, tB2, p2);
-  }
-  if ((rc = check_cuda(cudaGetLastError(), "moe_gemm_kernel launch"))) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kMoeThreads);
+  cfg.dynamicSmemBytes = PairCfg::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t le;
+  cfg.gridDim = dim3(2 * pairs1);
+  le = x_dtype == RB_BF16 ? cudaLaunchKernelEx(&cfg, moe_gemm_pair_kernel<1, __nv_bfloat16>, tA1, tB1, p1)
+                          : cudaLaunchKernelEx(&cfg, moe_gemm_pair_kernel<1, __half>, tA1, tB1, p1);
+  if (le != cudaSuccess) return check_cuda(le, "moe_gemm_pair_kernel<1> launch");
+  cfg.gridDim = dim3(2 * pairs2);
+  le = x_dtype == RB_BF16 ? cudaLaunchKernelEx(&cfg, moe_gemm_pair_kernel<2, __nv_bfloat16>, tA2, tB2, p2)
+                          : cudaLaunchKernelEx(&cfg, moe_gemm_pair_kernel<2, __half>, tA2, tB2, p2);
+  if (le != cudaSuccess) return check_cuda(le, "moe_gemm_pair_kernel<2> launch");
+  if ((rc = check_cuda(cudaGetLastError(), "moe_gemm_pair_kernel launch"))) return rc;
   if (idx_dtype == RB_I64) {
     if (x_dtype == RB_BF16)
       combine_kernel<__nv_bfloat16, int64_t><<<cgrid, 256, 0, st>>>(
