@@ -143,14 +143,14 @@ __global__ void __launch_bounds__(kRouteThreads) route_scatter_kernel(
       for (int w = 0; w < kWarps; ++w) add += s_wcnt[w][e2];
       s_next[e2] += add;
     }
-    // each warp copies the rows of its 32 entries, 16 bytes per lane, four
-    // rows (eight loads per lane) in flight at a time
+    // each warp copies the rows of its 32 entries, 16 bytes per lane, eight
+    // rows (sixteen loads per lane) in flight at a time
     for (int c0 = 0; c0 < chunks16; c0 += 64) {
-      for (int q0 = 0; q0 < 32; q0 += 4) {
-        uint4 v[4][2];
-        int pq[4];
+      for (int q0 = 0; q0 < 32; q0 += 8) {
+        uint4 v[8][2];
+        int pq[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 8; ++u) {
           const int t = warp * 32 + q0 + u;
           pq[u] = s_pos[t];
           const uint4* src = reinterpret_cast<const uint4*>(x + s_tok[t] * x_pitch);
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_scatter_kernel(
           }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 8; ++u) {
           uint4* dst = reinterpret_cast<uint4*>(packed + (int64_t)pq[u] * row_bytes);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -182,6 +182,39 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, c
   const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= Tn) return;
   const int lane = threadIdx.x & 31;
+  if (k == 2 && D == 512) {
+    // the SMoE's top-2 at d_model 512: both routes' ids, then all four 16-byte
+    // row pieces of the lane requested before any arithmetic
+    const int64_t v0 = (int64_t)idx[2 * t], v1 = (int64_t)idx[2 * t + 1];
+    const bool ok0 = v0 >= 0 && v0 < E, ok1 = v1 >= 0 && v1 < E;
+    const uint4* y0 = reinterpret_cast<const uint4*>(y + (2 * t) * (int64_t)512) + lane;
+    const uint4* y1 = reinterpret_cast<const uint4*>(y + (2 * t + 1) * (int64_t)512) + lane;
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+    uint4 w[2][2];
+    w[0][0] = ok0 ? __ldg(y0) : zero;
+    w[0][1] = ok0 ? __ldg(y0 + 32) : zero;
+    w[1][0] = ok1 ? __ldg(y1) : zero;
+    w[1][1] = ok1 ? __ldg(y1 + 32) : zero;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        if (!(s == 0 ? ok0 : ok1)) continue;
+        const T* hv = reinterpret_cast<const T*>(&w[s][h]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = (float)T(acc[i] + (float)hv[i]);
+      }
+      uint4 o;
+      T* oh = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) oh[i] = T(acc[i]);
+      *reinterpret_cast<uint4*>(out + t * ldo + 8 * lane + 256 * h) = o;
+    }
+    return;
+  }
   for (int c = lane * 8; c < D; c += 32 * 8) {
     float acc[8];
 #pragma unroll
