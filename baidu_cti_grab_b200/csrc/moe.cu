@@ -313,21 +313,22 @@ __device__ __forceinline__ void moe_epilogue_tile(const MoeGemmParams& p, int e,
   for (int c = c_begin; c < c_end; ++c) {
     const int col0 = n0 + c * 32;
     if (col0 >= p.N) break;  // warp-uniform
-    uint32_t r[32];
-    tc::tmem_ld32(t_acc + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32), r);
-    if (!live) continue;
-    // the chunk's 32 bias values: four 16-byte loads when aligned
+    // the chunk's 32 bias values (four 16-byte loads when aligned), requested
+    // before the TMEM load so that the two latencies overlap
     T bv[32];
     if (bias != nullptr) {
       const T* bp = bias + (int64_t)e * p.N + col0;
       if ((reinterpret_cast<uintptr_t>(bp) & 15) == 0 && col0 + 32 <= p.N) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(bv + 8 * q) = reinterpret_cast<const uint4*>(bp)[q];
+        for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(bv + 8 * q) = __ldg(reinterpret_cast<const uint4*>(bp) + q);
       } else {
 #pragma unroll
         for (int q = 0; q < 32; ++q) bv[q] = col0 + q < p.N ? bp[q] : T(0.0f);
       }
     }
+    uint32_t r[32];
+    tc::tmem_ld32(t_acc + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32), r);
+    if (!live) continue;
     uint32_t packed[16];
     if constexpr (std::is_same<T, __nv_bfloat16>::value) {
       if (bias != nullptr) {
