@@ -80,7 +80,7 @@ def w8a8_linear_triton_dynamic_unfused(x, weight_int8, weight_scale, bias=None, 
 def w8a8_linear_triton_dynamic_fused(x, weight_int8, weight_scale, bias=None, out_dtype=torch.bfloat16,
                                      block_m=32, block_n=64, block_k=64, group_m=8):
     """The reference's single-kernel variant: same arguments and the same output
-    bits as the two-kernel one, which this build runs for both (each row is
+    bits as the two-kernel one, which this library runs for both (each row is
     quantised once instead of once per output tile)."""
     return _linear_v1("w8a8_linear_triton_dynamic_fused", x, weight_int8, weight_scale, bias, out_dtype)
 

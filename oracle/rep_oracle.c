@@ -30,8 +30,8 @@
  *                           int8 quantiser once rstd is known (see below).
  *
  * LayerNorm order.  The reference's nn.LayerNorm runs ATen's CUDA kernel on
- * the GPU (PyTorch, not vendored by the reference: it pins torch 2.6.0 and
- * this build runs 2.11.0; aten/src/ATen/native/cuda/layer_norm_kernel.cu,
+ * the GPU (PyTorch, not vendored by the reference: it pins torch 2.6.0, and
+ * the tests here run 2.11.0; aten/src/ATen/native/cuda/layer_norm_kernel.cu,
  * vectorized_layer_norm_kernel -> compute_stats, taken for rows whose length
  * is a multiple of 4 with aligned buffers, which every RepEncoder row is).
  * Its published algorithm, restated:
