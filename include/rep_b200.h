@@ -221,7 +221,7 @@ int rb_w8a8_gemm(const int8_t* A, int64_t lda, const int8_t* B, int64_t ldb, int
  * rb_w8a8_gemm with a caller-provided int32 workspace: for mid M (from 257 rows
  * while the one-SM kernel's 128 x 256 tiles are fewer than the SMs, and from
  * 2048 rows while the two-SM kernel's 256 x 256 tiles cover at most half of the
- * CTA pairs; M up to about 4.7k at N = 512) the K dimension is split across
+ * CTA pairs; M up to 4608 at N = 512) the K dimension is split across
  * CTAs, each split's int32 partial goes to the workspace, and a second kernel
  * sums the splits (int32 addition is exact in any order) and applies the
  * epilogue.  Same results as rb_w8a8_gemm,

@@ -139,3 +139,33 @@ def test_table_row_count_above_int32_is_rejected():
     rc = lib.rb_rep_gather_pool_scatter(fake, _lib.RB_BF16, too_many, 512, vals, offs, nnz, cols, S, N,
                                         _lib.ptr_array([fake]), _lib.i64_array([0, N]), 1, S * 512, 0, None)
     assert rc == _lib.RB_ERR_VALUE and "num_rows" in _lib.last_error()
+
+
+def test_split_k_workspace_sizes():
+    """rb_w8a8_gemm_workspace_size (host logic; without a GPU the library
+    assumes a 148-SM B200): no workspace up to M = 256 (GEMV and the
+    swapped-operand cluster kernel) or once the CTA-pair tiles cover more than
+    half of the 74 pairs; K splits of the one-SM 128 x 256 tiles from M = 257,
+    of the pairs' 256 x 256 tiles from M = 2048; and never more int32 than the
+    20 MiB array of rb_w8a8_gemm_noalloc holds."""
+    from baidu_cti_grab_b200 import _lib
+
+    lib = _lib.load()
+    K, N = 14336, 512
+
+    def ws(M, n=N, k=K):
+        return int(lib.rb_w8a8_gemm_workspace_size(M, n, k))
+
+    for M in (1, 16, 17, 128, 256):
+        assert ws(M) == 0, M
+    assert ws(512) == 16 * 512 * N      # 8 one-SM tiles: 148 // 8 = 18 splits, capped at 16
+    assert ws(1024) == 9 * 1024 * N     # 16 tiles: 148 // 16 = 9 splits
+    assert ws(2048) == 4 * 2048 * N     # 16 pair tiles: 74 // 16 = 4 splits
+    assert ws(4096) == 2 * 4096 * N     # 32 pair tiles: 2 splits
+    assert ws(4608) == 2 * 4608 * N     # 36 pair tiles: still at most half of the pairs
+    for M in (4609, 8192, 32768, 103917):
+        assert ws(M) == 0, M
+    assert ws(0) == 0 and ws(4096, k=15) == 0  # empty, or K not a multiple of 16
+    scratch = 5 * 1024 * 1024
+    worst = max(ws(M) for M in range(1, 8193))
+    assert 0 < worst <= scratch
